@@ -1,0 +1,393 @@
+"""Benchmark of the B200 attention backend (one JSON line on stdout, rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+A step is one forward pass of the hot path over one batch of the workload's
+seeded synthetic inputs (shapes, seeds and value distributions of the
+portable-attention benchmark configurations, ``pa_b200.workloads``). The
+default workload is the fp16 causal grouped-query prefill forward, q
+(8, 32, 4096, 128), k/v (8, 8, 4096, 128): its inputs (512 MiB) exceed the
+126 MB L2, so no flush is needed between iterations.
+
+* ``value``: whole-job TFLOP/s (or GB/s for decode) with inputs resident in
+  HBM, timed with CUDA events on the launching stream over exactly K steps,
+  max over ranks.
+* ``e2e``: the same metric through the public SdpaBackend call on NumPy arrays
+  in page-locked host memory, host->device and device->host copies included.
+* ``roofline``: the dominant kernel's algorithmic FLOPs (bytes) per launch
+  over its average CUDA-event launch time, against MEASURED_PEAKS.json.
+* ``cpu_baseline``: the oracle port of the reference's ``fused`` CPU backend
+  on a bounded sample of the same workload, all host threads, BLAS pinned to
+  one thread per worker (rank 0, N=1 only).
+
+Multi-GPU (torchrun): batch x head shards are independent, so every rank
+runs its own copy of the workload (weak scaling, no data-path collective);
+torch.distributed provides only the barrier and the max-over-ranks timing.
+
+``--impl reference`` times the reference's CPU algorithm (the oracle port of
+``fused``) on the box's host cores on a bounded sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "portable-attention_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SDPA TFLOP/s (fwd, fwd+bwd) at 1/2/4/8 B200; decode HBM GB/s; %peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self._t is not None:
+                self._t.join(timeout=2)
+
+    def summary(self):
+        mhz, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, local, world, pg
+
+
+def barrier(pg):
+    if pg is not None:
+        pg.barrier()
+
+
+def max_over_ranks(pg, value: float, local: int) -> float:
+    if pg is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{local}")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU leg
+
+def cpu_sample(name, budget_s=12.0):
+    """Time the oracle port of ``fused`` on whole (batch, head) slices of the workload.
+
+    Returns (rate in the metric's unit, threads, description). Slices run in a
+    thread pool, one per host core, each with BLAS pinned to one thread.
+    """
+    import threadpoolctl
+
+    from oracle.sdpa import fused_sdpa
+    from pa_b200 import workloads
+
+    w = workloads.WORKLOADS[name]
+    x = workloads.make(name, batch_rows=slice(0, 1)) if name != "fp16_decode_gqa" else None
+    threads = os.cpu_count() or 1
+    group = w.q_shape[1] // w.kv_shape[1]
+    if name == "fp16_decode_gqa":
+        gen = np.random.default_rng(3)
+        q = (gen.standard_normal((1, w.q_shape[1], 1, w.q_shape[3])) * 0.5).astype(np.float16)
+        kv = [(gen.standard_normal((1, w.kv_shape[1], w.kv_shape[2], w.kv_shape[3])) * 0.5)
+              .astype(np.float16) for _ in range(2)]
+        jobs = [(q, kv[0], kv[1], {"enable_gqa": True})] * max(threads, 8)
+        unit_work = 2 * w.kv_shape[1] * w.kv_shape[2] * w.kv_shape[3] * 2  # K+V bytes per batch row
+    else:
+        jobs = []
+        L, S = w.q_shape[2], w.kv_shape[2]
+        for h in range(w.q_shape[1]):
+            kw = {}
+            if w.is_causal:
+                kw["is_causal"] = True
+            if w.masked:
+                kw["attn_mask"] = x["mask"][0, 0]
+            jobs.append((x["q"][0, h], x["k"][0, h // group], x["v"][0, h // group], kw))
+        unit_work = 4.0 * L * S * w.q_shape[3] * (0.5 if w.is_causal else 1.0)
+    done = 0
+    t0 = time.perf_counter()
+    with threadpoolctl.threadpool_limits(limits=1), ThreadPoolExecutor(threads) as ex:
+        while True:
+            batch = jobs[: max(threads, 1)]
+            list(ex.map(lambda j: fused_sdpa(j[0], j[1], j[2], **j[3]), batch))
+            done += len(batch)
+            if time.perf_counter() - t0 > budget_s or done >= 4 * threads:
+                break
+    dt = time.perf_counter() - t0
+    rate = done * unit_work / dt
+    if name == "fp16_decode_gqa":
+        return rate / 1e9, threads, f"{done} batch rows of q (1,32,1,128) vs k/v (1,8,32768,128), {dt:.1f}s"
+    return rate / 1e12, threads, f"{done} (b,h) slices of the workload, {dt:.1f}s wall"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from pa_b200 import workloads
+
+    w = workloads.WORKLOADS[args.workload]
+    rates = []
+    for i in range(args.warmup + args.steps):
+        rate, threads, desc = cpu_sample(args.workload, budget_s=4.0)
+        if i >= args.warmup:
+            rates.append(rate)
+    value = statistics.median(rates)
+    unit = "GB/s" if args.workload == "fp16_decode_gqa" else "TFLOP/s"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if w.dtype == "float16" else w.dtype.replace("float", "f"),
+        "data": "synthetic", "config": workload_config(args.workload, args.gpus),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
+                         "sample": desc + " per step; oracle port of the fused backend"},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(name, n):
+    from pa_b200 import workloads
+
+    w = workloads.WORKLOADS[name]
+    return {"workload": f"{name}: q {w.q_shape} k/v {w.kv_shape} {w.dtype}"
+                        f"{' causal' if w.is_causal else ''}{' gqa' if w.enable_gqa else ''}"
+                        f"{' key-padding mask' if w.masked else ''}",
+            "global_batch": w.q_shape[0] * n, "seq_len": w.q_shape[2],
+            "parallelism": f"batch-shard x{n}" if n > 1 else "single",
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+# ---------------------------------------------------------------- GPU leg
+
+def run_gpu(args):
+    rank, local, world, pg = dist_setup(args.gpus)
+    import pa_b200
+    from pa_b200 import workloads
+    from pa_b200.backend import sdpa_device, use_decode_kernel
+    from pa_b200.device import DeviceBuffer, Event, Stream
+
+    pa_b200.set_device(local)
+    w = workloads.WORKLOADS[args.workload]
+    x = workloads.make(args.workload)
+    mask = x.get("mask")
+    plan = pa_b200.plan_call(x["q"].shape, x["k"].shape, x["v"].shape, x["q"].dtype, x["k"].dtype,
+                             x["v"].dtype, None if mask is None else mask.shape,
+                             None if mask is None else mask.dtype, w.is_causal, None,
+                             w.q_shape[1] // w.kv_shape[1])
+    decode = use_decode_kernel(plan)
+    stream = Stream()
+    bufs = {}
+    from pa_b200._lib import check, lib
+
+    for key in ("q", "k", "v"):
+        a = np.ascontiguousarray(x[key])
+        bufs[key] = DeviceBuffer(a.nbytes)
+        check(lib().pa_memcpy_h2d(bufs[key].ptr, a.ctypes.data, a.nbytes, stream.handle))
+    if mask is not None:
+        m = np.ascontiguousarray(mask).view(np.uint8)
+        bufs["mask"] = DeviceBuffer(m.nbytes)
+        check(lib().pa_memcpy_h2d(bufs["mask"].ptr, m.ctypes.data, m.nbytes, stream.handle))
+    out_bytes = int(np.prod(plan.out_shape)) * plan.cdt.itemsize
+    bufs["out"] = DeviceBuffer(out_bytes)
+    stream.synchronize()
+
+    def step():
+        sdpa_device(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["out"].ptr,
+                    mask_ptr=bufs["mask"].ptr if "mask" in bufs else None, stream=stream,
+                    decode=decode)
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    pa_b200.sync_device_status()
+    events = [Event() for _ in range(args.steps + 1)]
+    barrier(pg)
+    stream.synchronize()
+    with ClockSampler(local) as clocks:
+        events[0].record(stream)
+        for i in range(args.steps):
+            step()
+            events[i + 1].record(stream)
+        stream.synchronize()
+    barrier(pg)
+    pa_b200.sync_device_status()
+    per = [events[i].elapsed_ms(events[i + 1]) for i in range(args.steps)]
+    ms_local = events[0].elapsed_ms(events[-1]) / args.steps
+    ms = max_over_ranks(pg, ms_local, local)
+
+    pk, pk_kind = peaks()
+    if decode:
+        unit = "GB/s"
+        work = float(2 * x["k"].nbytes + x["q"].nbytes + out_bytes)
+        value = world * work / (ms * 1e-3) / 1e9
+        achieved = work / (statistics.mean(per) * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": traffic_for(args.workload),
+                "peak_kind": pk_kind, "kernel": "decode_splitkv"}
+    else:
+        unit = "TFLOP/s"
+        work = w.flops_fwd
+        value = world * work / (ms * 1e-3) / 1e12
+        achieved = work / (statistics.mean(per) * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                "traffic": traffic_for(args.workload), "peak_kind": pk_kind + " (burst)",
+                "kernel": "fwd_tc"}
+
+    # End to end through the public call on page-locked NumPy inputs.
+    hq = pa_b200.pinned_empty(x["q"].shape, x["q"].dtype)
+    hk = pa_b200.pinned_empty(x["k"].shape, x["k"].dtype)
+    hv = pa_b200.pinned_empty(x["v"].shape, x["v"].dtype)
+    hq[...], hk[...], hv[...] = x["q"], x["k"], x["v"]
+    kw = {"is_causal": w.is_causal, "enable_gqa": w.enable_gqa}
+    if mask is not None:
+        kw["attn_mask"] = mask
+    for _ in range(max(1, min(args.warmup, 2))):
+        pa_b200.scaled_dot_product_attention(hq, hk, hv, **kw)
+    e2e_steps = max(1, min(args.steps, 5))
+    barrier(pg)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        res = pa_b200.scaled_dot_product_attention(hq, hk, hv, **kw)
+    e2e_ms_local = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    barrier(pg)
+    e2e_ms = max_over_ranks(pg, e2e_ms_local, local)
+    e2e_val = world * work / (e2e_ms * 1e-3) / (1e9 if decode else 1e12)
+    h2d = hq.nbytes + hk.nbytes + hv.nbytes + (mask.nbytes if mask is not None else 0)
+    d2h = res.nbytes
+
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": workload_config(args.workload, world),
+        "roofline": roof,
+        "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
+                "timing": "host wall clock around the synchronous public call"},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        rate, threads, desc = cpu_sample(args.workload)
+        line["cpu_baseline"] = {"value": rate, "unit": unit, "cores": threads, "kind": "port",
+                                "sample": desc + "; oracle port of the fused backend"}
+    print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+def traffic_for(name):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        return json.loads(p.read_text()).get(name)
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="fp16_causal_gqa")
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

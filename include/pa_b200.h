@@ -1,0 +1,195 @@
+/*
+ * pa_b200.h -- C ABI of the B200 (sm_100a) attention library libpa_b200.so.
+ *
+ * This is the drop-in boundary for the portable-attention backend seam: the
+ * Python host layer (package pa_b200) binds every symbol here through ctypes
+ * and registers the result with portable_attention.register_backend
+ * (src/portable_attention/dispatch.py:92-120) as an SdpaBackend
+ * (dispatch.py:53-76). Any other FFI (cffi, JNI, cgo) can bind the same
+ * symbols: only plain pointers, sizes and the POD descriptor below cross it.
+ *
+ * Conventions
+ *  - Every entry point returns a pa_status (0 = PA_OK). On failure a
+ *    thread-local message is available from pa_last_error(); no C++ exception
+ *    crosses the boundary.
+ *  - Device pointers come from pa_malloc (or any CUDA allocation on the
+ *    current device). A NULL stream means the legacy default stream.
+ *  - Compute entry points are asynchronous on `stream`; pa_stream_sync or the
+ *    synchronous copy helpers complete them. Kernels whose bounded waits give
+ *    up record a code in a per-device status word read by pa_device_status.
+ *  - Element strides are in elements, not bytes.
+ */
+#ifndef PA_B200_H
+#define PA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t pa_status;
+enum {
+  PA_OK = 0,
+  PA_ERR_INVALID = 1,     /* bad argument: mirrors the reference's ValueError */
+  PA_ERR_UNSUPPORTED = 2, /* valid input this library does not handle (dropout...) */
+  PA_ERR_CUDA = 3,        /* a CUDA runtime / driver call failed */
+  PA_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up */
+  PA_ERR_NCCL = 5,        /* an NCCL call failed or a peer timed out */
+  PA_ERR_NOMEM = 6        /* device or pinned-host allocation failed */
+};
+
+/* Element types. */
+enum { PA_F16 = 1, PA_BF16 = 2, PA_F32 = 3, PA_F64 = 4, PA_BOOL = 5 };
+
+/* Mask kinds: none, boolean keep-mask (1 byte per element, nonzero = keep),
+ * additive float mask (type mask_dtype) added to the scaled scores. */
+enum { PA_MASK_NONE = 0, PA_MASK_BOOL = 1, PA_MASK_ADD = 2 };
+
+#define PA_MAX_LEAD 6
+
+/*
+ * Problem descriptor for one scaled-dot-product-attention call.
+ *
+ * Shapes follow the reference contract (src/portable_attention/reference.py:76-82):
+ * query (*, L, E), key (*, S, E), value (*, S, Ev) -> out (*, L, Ev), with the
+ * leading dims `lead[0..nlead)` being the broadcast leading shape of the
+ * output. Each operand gives one element stride per leading dim (0 where it
+ * broadcasts) and a row stride; its last dim is contiguous. `out` is always
+ * dense: out[(slice * L + i) * Ev + j], slice = row-major index over `lead`.
+ *
+ * Grouped-query attention (reference.py:20-53): when gqa_group > 1, key and
+ * value are indexed along leading dim `gqa_axis` by (query index / gqa_group).
+ *
+ * Causal masking is top-left aligned: key j is visible to query i iff j <= i
+ * (reference.py:141-144). A mask has one element stride per leading dim plus
+ * row and column strides (column stride may be 0 for a broadcast column).
+ */
+typedef struct pa_sdpa_desc {
+  int32_t dtype;                      /* PA_F16 / PA_BF16 / PA_F32 / PA_F64 for q,k,v,out */
+  int32_t nlead;                      /* 0..PA_MAX_LEAD */
+  int64_t lead[PA_MAX_LEAD];
+  int64_t q_lead_stride[PA_MAX_LEAD];
+  int64_t k_lead_stride[PA_MAX_LEAD];
+  int64_t v_lead_stride[PA_MAX_LEAD];
+  int64_t m_lead_stride[PA_MAX_LEAD];
+  int64_t L, S, E, Ev;
+  int64_t q_row_stride, k_row_stride, v_row_stride;
+  int32_t gqa_axis;                   /* -1 when gqa_group == 1 */
+  int32_t gqa_group;                  /* Hq / Hkv, >= 1 */
+  int32_t mask_kind;                  /* PA_MASK_* */
+  int32_t mask_dtype;                 /* PA_BOOL, or PA_F16/PA_F32/PA_F64 for additive */
+  int64_t m_row_stride, m_col_stride;
+  int32_t is_causal;
+  int32_t reserved;
+  double scale;                       /* softmax scale (caller resolves the 1/sqrt(E) default) */
+} pa_sdpa_desc;
+
+/* ---- library / device ------------------------------------------------- */
+
+/* Library version as major*10000 + minor*100 + patch. */
+int32_t pa_version(void);
+/* Thread-local text of the last failure on this thread ("" if none). */
+const char* pa_last_error(void);
+/* Initialise the runtime and report the visible CUDA device count (0 on a
+ * host without a usable GPU, with PA_ERR_CUDA). */
+pa_status pa_init(int32_t* ndev);
+pa_status pa_set_device(int32_t dev);
+pa_status pa_get_device(int32_t* dev);
+/* Read and clear the device status word of the current device: 0, or the
+ * code of a bounded device-side wait that gave up (implies PA_ERR_TIMEOUT). */
+pa_status pa_device_status(int32_t* code);
+
+/* ---- memory and streams ------------------------------------------------ */
+
+pa_status pa_malloc(void** dptr, size_t bytes);
+pa_status pa_free(void* dptr);
+pa_status pa_host_alloc(void** hptr, size_t bytes); /* page-locked host memory */
+pa_status pa_host_free(void* hptr);
+pa_status pa_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+pa_status pa_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+pa_status pa_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+pa_status pa_memset(void* dptr, int32_t value, size_t bytes, void* stream);
+pa_status pa_stream_create(void** stream);
+pa_status pa_stream_destroy(void* stream);
+pa_status pa_stream_sync(void* stream);
+pa_status pa_event_create(void** event);
+pa_status pa_event_destroy(void* event);
+pa_status pa_event_record(void* event, void* stream);
+pa_status pa_event_elapsed_ms(void* start, void* stop, float* ms);
+
+/* ---- attention ---------------------------------------------------------- */
+
+/*
+ * Forward attention. Replaces the backend call of
+ * src/portable_attention/dispatch.py:53-76 (SdpaBackend.__call__), whose
+ * CPU implementations are reference.py:56-163 and fused.py:115-218.
+ *
+ * `lse` (optional, may be NULL) receives the natural-log log-sum-exp of the
+ * scaled, masked scores per output row (float32, dense over lead x L);
+ * fully-masked rows get -inf and an exactly-zero output row
+ * (reference.py:151-160).
+ *
+ * Kernel choice is internal: fp16/bf16 with E == Ev in {64, 128} and dense
+ * (B, H, L, E) operands runs the tcgen05/TMEM tensor-core kernel; everything
+ * else runs the exact CUDA-core kernel (fp32 math for fp16/fp32, fp64 math
+ * for fp64; no TF32).
+ */
+pa_status pa_sdpa_fwd(const pa_sdpa_desc* desc, const void* q, const void* k, const void* v,
+                      const void* mask, void* out, float* lse, void* stream);
+
+/*
+ * Split-KV decode forward for L == 1 (no reference counterpart beyond the
+ * same SdpaBackend call with a length-1 query: dispatch.py:53-76). Dense
+ * (B, Hq, 1, D) query, (B, Hkv, S, D) key/value, D in {64, 128}, fp16/bf16,
+ * no mask, not causal. `workspace` holds the per-split partial results; pass
+ * NULL to let the library take it from its stream-ordered pool, or a buffer
+ * of at least pa_decode_workspace_size() bytes.
+ */
+pa_status pa_decode_workspace_size(const pa_sdpa_desc* desc, size_t* bytes);
+pa_status pa_decode_fwd(const pa_sdpa_desc* desc, const void* q, const void* k, const void* v,
+                        void* out, float* lse, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/*
+ * Backward (VJP) of pa_sdpa_fwd: dQ, dK, dV from q, k, v, the forward output,
+ * its cotangent dout and the forward's lse. The reference has no backward
+ * (the autograd hook is a roadmap item, ROADMAP.md:57-58); this is the
+ * gradient of reference.py:56-163. Dense (B, H, L, E) operands; dK/dV are
+ * summed over each grouped-query group. fp16/bf16 with E == Ev in {64, 128}
+ * run on tcgen05; fp32/fp64 run on CUDA cores.
+ */
+pa_status pa_sdpa_bwd(const pa_sdpa_desc* desc, const void* q, const void* k, const void* v,
+                      const void* out, const void* dout, const float* lse, void* dq, void* dk,
+                      void* dv, void* stream);
+
+/* ---- multi-GPU ---------------------------------------------------------- */
+
+typedef struct pa_comm pa_comm;
+
+/* 128-byte NCCL unique id made on one rank and shared out of band. */
+pa_status pa_comm_unique_id(uint8_t id[128]);
+pa_status pa_comm_init(pa_comm** comm, const uint8_t id[128], int32_t nranks, int32_t rank);
+pa_status pa_comm_destroy(pa_comm* comm);
+
+/*
+ * Ring (context-parallel) causal attention over `comm`. Each rank holds its
+ * zig-zag shard of the sequence: chunks r and 2n-1-r of 2n equal chunks, laid
+ * out back to back as (B, H, 2*C, D). K/V shards travel around the ring with
+ * NCCL send/recv on a side stream while the local block is computed; partial
+ * results merge by log-sum-exp. No reference counterpart (the reference has
+ * no distributed code); the result equals reference.py:56-163 on the gathered
+ * sequence.
+ */
+pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* local_desc, const void* q,
+                      const void* k, const void* v, void* out, float* lse, void* stream);
+pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* local_desc, const void* q,
+                      const void* k, const void* v, const void* out, const void* dout,
+                      const float* lse, void* dq, void* dk, void* dv, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PA_B200_H */

@@ -1,0 +1,23 @@
+// Internal launcher declarations shared by the C-ABI entry points.
+#pragma once
+
+#include "common.cuh"
+
+namespace pa {
+
+pa_status launch_fwd_exact(const pa_sdpa_desc& d, const void* q, const void* k, const void* v,
+                           const void* mask, void* out, float* lse, cudaStream_t st);
+
+// Dense (B, H, L, D) fp16/bf16 operands, D in {64, 128}.
+bool fwd_tc_eligible(const pa_sdpa_desc& d, std::string* why);
+pa_status launch_fwd_tc(const pa_sdpa_desc& d, const void* q, const void* k, const void* v,
+                        const void* mask, void* out, float* lse, cudaStream_t st);
+
+// Fill out with zeros and lse with -inf (S == 0: every row fully masked).
+pa_status launch_fill_dead(const pa_sdpa_desc& d, void* out, float* lse, cudaStream_t st);
+
+// True when q/k/v are dense (B..., H, rows, D) with grouped heads on the last
+// leading axis; reports the flattened slice count and head counts.
+bool dense_bhsd(const pa_sdpa_desc& d, int64_t* slices, int64_t* heads, int64_t* kv_heads);
+
+}  // namespace pa
