@@ -60,61 +60,77 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples during the timed region."""
+    """nvidia-smi clock / throttle samples (every 20 ms, to a file) around the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Sampling starts before warm-up (nvidia-smi takes a moment to start) and
+    :meth:`mark` brackets the timed region; the summary keeps the samples
+    inside it, or the nearest ones when the region is shorter than a period.
+    """
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, path: Path):
         self.index = index
+        self.path = path
         self.proc = None
-        self.lines: list[str] = []
-        self._t = None
+        self.window = [None, None]
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
-            self._t.start()
+                 "--format=csv,noheader,nounits", "-lms", "20", "-f", str(self.path)],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        time.sleep(0.3)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def mark(self, which: int):
+        self.window[which] = time.time()
 
-    def __exit__(self, *exc):
+    def stop(self):
         if self.proc is not None:
+            time.sleep(0.05)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-            if self._t is not None:
-                self._t.join(timeout=2)
 
     def summary(self):
-        mhz, mx, reasons = [], None, set()
+        import datetime
+
+        rows = []
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
+        try:
+            text = self.path.read_text()
+        except OSError:
+            text = ""
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                mhz.append(float(parts[1]))
-                mx = float(parts[2])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]), float(parts[4]),
+                             [n for n, v in zip(names, parts[6:10]) if v.lower() == "active"]))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(mhz)}
+        t0, t1 = self.window
+        inside = [r for r in rows if t0 is not None and t0 - 0.02 <= r[0] <= (t1 or t0) + 0.02]
+        how = "inside timed region"
+        if not inside and rows and t0 is not None:
+            inside = sorted(rows, key=lambda r: abs(r[0] - t0))[:3]
+            how = "nearest samples (timed region shorter than the 20 ms period)"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": inside[0][2],
+                "power_w_max": max(r[3] for r in inside),
+                "reasons": sorted({n for r in inside for n in r[4]}), "samples": len(inside),
+                "window": how}
 
 
 def dist_setup(n_gpus):
@@ -282,6 +298,9 @@ def run_gpu(args):
                     mask_ptr=bufs["mask"].ptr if "mask" in bufs else None, stream=stream,
                     decode=decode)
 
+    out_dir = ROOT / "gpurun_out"
+    out_dir.mkdir(exist_ok=True)
+    clocks = ClockSampler(local, out_dir / f"clocks_rank{rank}.csv").start()
     for _ in range(args.warmup):
         step()
     stream.synchronize()
@@ -289,12 +308,14 @@ def run_gpu(args):
     events = [Event() for _ in range(args.steps + 1)]
     barrier(pg)
     stream.synchronize()
-    with ClockSampler(local) as clocks:
-        events[0].record(stream)
-        for i in range(args.steps):
-            step()
-            events[i + 1].record(stream)
-        stream.synchronize()
+    clocks.mark(0)
+    events[0].record(stream)
+    for i in range(args.steps):
+        step()
+        events[i + 1].record(stream)
+    stream.synchronize()
+    clocks.mark(1)
+    clocks.stop()
     barrier(pg)
     pa_b200.sync_device_status()
     per = [events[i].elapsed_ms(events[i + 1]) for i in range(args.steps)]
@@ -376,7 +397,7 @@ def traffic_for(name):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="fp16_causal_gqa")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
