@@ -374,7 +374,7 @@ def run_gpu(args):
         "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
                 "timing": "host wall clock around the synchronous public call"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if decode else 1),
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu:

@@ -5,6 +5,9 @@
 
 namespace pa {
 
+// Structural checks of a descriptor shared by every entry point.
+pa_status check_desc(const pa_sdpa_desc* d);
+
 pa_status launch_fwd_exact(const pa_sdpa_desc& d, const void* q, const void* k, const void* v,
                            const void* mask, void* out, float* lse, cudaStream_t st);
 

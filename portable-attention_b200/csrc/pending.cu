@@ -4,14 +4,6 @@
 using namespace pa;
 
 extern "C" {
-pa_status pa_decode_workspace_size(const pa_sdpa_desc*, size_t* bytes) {
-  if (bytes) *bytes = 0;
-  return fail(PA_ERR_UNSUPPORTED, "pa_decode_fwd is not built yet");
-}
-pa_status pa_decode_fwd(const pa_sdpa_desc*, const void*, const void*, const void*, void*, float*,
-                        void*, size_t, void*) {
-  return fail(PA_ERR_UNSUPPORTED, "pa_decode_fwd is not built yet");
-}
 pa_status pa_sdpa_bwd(const pa_sdpa_desc*, const void*, const void*, const void*, const void*,
                       const void*, const float*, void*, void*, void*, void*) {
   return fail(PA_ERR_UNSUPPORTED, "pa_sdpa_bwd is not built yet");
