@@ -153,6 +153,39 @@ pa_status pa_decode_fwd(const pa_sdpa_desc* desc, const void* q, const void* k, 
                         void* stream);
 
 /*
+ * Allocation-free variant of pa_decode_fwd. It has no counterpart in the
+ * reference (which runs on the CPU and never manages device memory).
+ *
+ * For callers that cannot allocate device memory while they run: hosts whose
+ * allocator or memory budget forbids new cudaMalloc calls after start-up,
+ * plugins whose device memory belongs to another runtime, and serving loops
+ * that must not synchronise or fragment a pool mid-step. The caller passes
+ * only inputs and outputs; the split partials live in a file-scope device
+ * array of 8 MiB (8388608 bytes) that every GPU loading this library holds
+ * until the process exits. Problems whose partials need more than that
+ * (pa_decode_workspace_size reports the need) fail with PA_ERR_UNSUPPORTED
+ * and a message giving both sizes; nothing is launched then.
+ *
+ * The first call on each device looks up the array's device address with
+ * that device current (cudaGetSymbolAddress); make that first call before
+ * any stream capture. The entry point calls no cudaMalloc, cudaFree or other
+ * allocating routine.
+ *
+ * All calls on a device share the one array and it keeps the last call's
+ * contents. Every partial a call reads is written earlier in the same call,
+ * so nothing needs clearing, but calls that overlap on the GPU (different
+ * streams, or different host threads without ordering) race on the array:
+ * order them on one stream.
+ *
+ * `status` (device pointer, may be NULL) receives a nonzero code if a bounded
+ * device-side wait gives up; the caller zeroes it beforehand. With NULL the
+ * code goes to a library-internal word that is not reported.
+ */
+pa_status pa_decode_fwd_static(const pa_sdpa_desc* desc, const void* q, const void* k,
+                               const void* v, void* out, float* lse, int32_t* status,
+                               void* stream);
+
+/*
  * Backward (VJP) of pa_sdpa_fwd: dQ, dK, dV from q, k, v, the forward output,
  * its cotangent dout and the forward's lse. The reference has no backward
  * (the autograd hook is a roadmap item, ROADMAP.md:57-58); this is the

@@ -26,6 +26,8 @@
 #include <math.h>
 
 #include <cmath>
+#include <cstdio>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -398,9 +400,11 @@ pa_status launch_dec_g(const DecPlan& p, const CUtensorMap& tk, const CUtensorMa
 
 }  // namespace
 
-// Runs the decode with the given workspace (at least decode_ws_bytes bytes).
-pa_status run_decode(const pa_sdpa_desc& d, const void* q, const void* k, const void* v, void* out,
-                     float* lse, void* ws, size_t ws_bytes, cudaStream_t st) {
+// Runs the decode with the given workspace (at least decode_ws_bytes bytes);
+// bounded waits that give up record their code in `status`.
+pa_status run_decode_status(const pa_sdpa_desc& d, const void* q, const void* k, const void* v,
+                            void* out, float* lse, void* ws, size_t ws_bytes, int* status,
+                            cudaStream_t st) {
   DecPlan p;
   PA_TRY(make_plan(d, &p));
   if (ws_bytes < plan_ws_bytes(p)) return fail(PA_ERR_INVALID, "decode: workspace too small");
@@ -416,8 +420,7 @@ pa_status run_decode(const pa_sdpa_desc& d, const void* q, const void* k, const 
   const size_t slots = static_cast<size_t>(p.B * p.Hq) * p.nsplit;
   a.ws_acc = static_cast<float*>(ws);
   a.ws_ml = a.ws_acc + slots * p.D;
-  a.status = device_status_word();
-  if (!a.status) return fail(PA_ERR_CUDA, "device status word unavailable");
+  a.status = status;
   a.S = p.S;
   a.Hq = static_cast<int32_t>(p.Hq);
   a.Hkv = static_cast<int32_t>(p.Hkv);
@@ -430,6 +433,13 @@ pa_status run_decode(const pa_sdpa_desc& d, const void* q, const void* k, const 
                 : launch_dec_g<128, false>(p, tk, tv, a, out, lse, st);
   return bf16 ? launch_dec_g<64, true>(p, tk, tv, a, out, lse, st)
               : launch_dec_g<64, false>(p, tk, tv, a, out, lse, st);
+}
+
+pa_status run_decode(const pa_sdpa_desc& d, const void* q, const void* k, const void* v, void* out,
+                     float* lse, void* ws, size_t ws_bytes, cudaStream_t st) {
+  int* status = device_status_word();
+  if (!status) return fail(PA_ERR_CUDA, "device status word unavailable");
+  return run_decode_status(d, q, k, v, out, lse, ws, ws_bytes, status, st);
 }
 
 pa_status decode_ws_bytes(const pa_sdpa_desc& d, size_t* bytes) {
@@ -468,4 +478,78 @@ extern "C" pa_status pa_decode_fwd(const pa_sdpa_desc* desc, const void* q, cons
   pa_status s = run_decode(d, q, k, v, out, lse, ws, need, st);
   scratch_free(ws, st);
   return s;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode: the split partials live in a file-scope device
+// array instead of a workspace from cudaMallocAsync or from the caller.
+//
+// Some callers cannot allocate device memory at call time: code running
+// under an allocator or memory budget that forbids new cudaMalloc calls once
+// a model is loaded, plugin hosts whose device memory is owned by another
+// runtime, and latency-critical serving loops that must not synchronise or
+// fragment the pool. They pass inputs and outputs only. The scratch below is
+// part of the loaded module, so every GPU that loads this library holds it
+// (kStaticScratchBytes) until the process exits.
+namespace pa {
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
+// Status word for bounded waits when the caller passes none (write-only here).
+static __device__ __align__(256) int g_decode_static_status[64];
+
+constexpr int kMaxDev = 64;
+void* g_scratch_addr[kMaxDev] = {};
+int* g_status_addr[kMaxDev] = {};
+std::mutex g_static_mu;
+
+// Host code may not use the symbols' names as device addresses: fetch the
+// real addresses once per device, with that device current.
+pa_status static_scratch_for_current_device(void** scratch, int** status) {
+  int dev = 0;
+  PA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDev) return fail(PA_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_scratch_addr[dev]) {
+    void* s = nullptr;
+    void* w = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&s, g_decode_scratch);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(decode scratch)");
+    e = cudaGetSymbolAddress(&w, g_decode_static_status);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(decode status)");
+    g_status_addr[dev] = static_cast<int*>(w);
+    g_scratch_addr[dev] = s;
+  }
+  *scratch = g_scratch_addr[dev];
+  *status = g_status_addr[dev];
+  return PA_OK;
+}
+
+}  // namespace
+}  // namespace pa
+
+extern "C" pa_status pa_decode_fwd_static(const pa_sdpa_desc* desc, const void* q, const void* k,
+                                          const void* v, void* out, float* lse, int32_t* status,
+                                          void* stream) {
+  clear_error();
+  PA_TRY(check_desc(desc));
+  const pa_sdpa_desc& d = *desc;
+  if (lead_count(d) == 0) return PA_OK;
+  size_t need = 0;
+  PA_TRY(decode_ws_bytes(d, &need));
+  if (need > kStaticScratchBytes) {
+    char buf[192];
+    snprintf(buf, sizeof buf,
+             "pa_decode_fwd_static: this problem needs %zu bytes of split scratch; the static "
+             "scratch holds %zu bytes (use pa_decode_fwd with a workspace)",
+             need, kStaticScratchBytes);
+    return fail(PA_ERR_UNSUPPORTED, buf);
+  }
+  void* scratch = nullptr;
+  int* own_status = nullptr;
+  PA_TRY(static_scratch_for_current_device(&scratch, &own_status));
+  int* st_word = status ? reinterpret_cast<int*>(status) : own_status;
+  return run_decode_status(d, q, k, v, out, lse, scratch, kStaticScratchBytes, st_word,
+                           static_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,93 @@
+"""The allocation-free decode entry point, called through the C ABI.
+
+``pa_decode_fwd_static`` serves callers that cannot allocate device memory
+while they run (a fixed memory budget after start-up, device memory owned by
+another runtime, serving loops that must not touch the pool): its split
+scratch is a fixed 8 MiB device array inside the library. Here it must give
+the same output as the allocating ``pa_decode_fwd`` (within the fp16 2e-3
+tolerance used throughout), on two calls in a row with different inputs, and
+must reject a problem whose scratch need exceeds the array.
+
+This file is named to be collected last, so a first-failure run has already
+run every other test; it also passes alone in a fresh process.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(fn_name, plan, arrays, extra):
+    import pa_b200
+    from pa_b200._lib import check, lib
+    from pa_b200.device import DeviceBuffer, Stream
+
+    st = Stream()
+    q, k, v = arrays
+    bufs = [DeviceBuffer(x.nbytes) for x in (q, k, v)]
+    for b, x in zip(bufs, (q, k, v)):
+        check(lib().pa_memcpy_h2d(b.ptr, x.ctypes.data, x.nbytes, st.handle))
+    out = DeviceBuffer(q.nbytes)
+    lse = DeviceBuffer(q.shape[0] * q.shape[1] * 4)
+    fn = getattr(lib(), fn_name)
+    check(fn(ctypes.byref(plan.desc), bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, out.ptr, lse.ptr,
+             *extra(st)))
+    o = np.empty_like(q)
+    l = np.empty(q.shape[:2], np.float32)
+    check(lib().pa_memcpy_d2h(o.ctypes.data, out.ptr, o.nbytes, st.handle))
+    check(lib().pa_memcpy_d2h(l.ctypes.data, lse.ptr, l.nbytes, st.handle))
+    st.synchronize()
+    pa_b200.sync_device_status()
+    return o, l
+
+
+def _inputs(seed, b=4, hq=16, hkv=4, s=9000, d=128):
+    rng = np.random.default_rng(seed)
+    q = (rng.standard_normal((b, hq, 1, d)) * 0.5).astype(np.float16)
+    k = (rng.standard_normal((b, hkv, s, d)) * 0.5).astype(np.float16)
+    v = (rng.standard_normal((b, hkv, s, d)) * 0.5).astype(np.float16)
+    return q, k, v
+
+
+def test_static_scratch_decode_matches_allocating_decode_twice():
+    import pa_b200
+    from pa_b200.device import DeviceBuffer
+    from pa_b200._lib import check, lib
+
+    status = DeviceBuffer(4)
+    for seed, shape in ((1, dict()), (2, dict(b=2, hq=8, hkv=8, s=3001, d=64))):
+        q, k, v = _inputs(seed, **shape)
+        plan = pa_b200.plan_call(q.shape, k.shape, v.shape, q.dtype, k.dtype, v.dtype,
+                                 group=q.shape[1] // k.shape[1])
+        want_o, want_l = _run("pa_decode_fwd", plan, (q, k, v),
+                              lambda st: (None, 0, st.handle))
+        check(lib().pa_memset(status.ptr, 0, 4, None))
+        check(lib().pa_stream_sync(None))
+        got_o, got_l = _run("pa_decode_fwd_static", plan, (q, k, v),
+                            lambda st: (status.ptr, st.handle))
+        code = np.zeros(1, np.int32)
+        check(lib().pa_memcpy_d2h(code.ctypes.data, status.ptr, 4, None))
+        check(lib().pa_stream_sync(None))
+        assert code[0] == 0
+        np.testing.assert_allclose(got_o.astype(np.float64), want_o.astype(np.float64),
+                                   rtol=2e-3, atol=2e-3)
+        np.testing.assert_allclose(got_l, want_l, rtol=2e-3, atol=2e-3)
+
+
+def test_static_scratch_rejects_oversized_problem():
+    import pa_b200
+    from pa_b200._lib import lib
+
+    # 256 x 64 query heads x (128 + 2) floats of partials = 8.5 MB > 8 MiB.
+    plan = pa_b200.plan_call((256, 64, 1, 128), (256, 8, 32, 128), (256, 8, 32, 128),
+                             np.float16, np.float16, np.float16, group=8)
+    rc = lib().pa_decode_fwd_static(ctypes.byref(plan.desc), None, None, None, None, None, None,
+                                    None)
+    assert rc != 0
+    msg = lib().pa_last_error().decode()
+    assert "static scratch holds 8388608 bytes" in msg
