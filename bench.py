@@ -170,11 +170,15 @@ def max_over_ranks(pg, value: float, local: int) -> float:
 
 # ---------------------------------------------------------------- CPU leg
 
-def cpu_sample(name, budget_s=12.0):
-    """Time the oracle port of ``fused`` on whole (batch, head) slices of the workload.
+def cpu_sample(name, budget_s=12.0, x=None):
+    """Time the oracle port of ``fused`` on a bounded sample of the workload.
 
-    Returns (rate in the metric's unit, threads, description). Slices run in a
-    thread pool, one per host core, each with BLAS pinned to one thread.
+    Returns (rate in the metric's unit, threads, description). Work items run
+    in a thread pool, one per host core, each with BLAS pinned to one thread.
+    Items are whole (batch, head) slices, except for decode (whole batch
+    rows) and the 131072-long causal workload (64-row query blocks against
+    the keys they see, with the causal mask as an explicit boolean slice);
+    the reference has no backward, so that baseline is forward-only.
     """
     import threadpoolctl
 
@@ -182,41 +186,57 @@ def cpu_sample(name, budget_s=12.0):
     from pa_b200 import workloads
 
     w = workloads.WORKLOADS[name]
-    x = workloads.make(name, batch_rows=slice(0, 1)) if name != "fp16_decode_gqa" else None
     threads = os.cpu_count() or 1
     group = w.q_shape[1] // w.kv_shape[1]
+    D = w.q_shape[3]
     if name == "fp16_decode_gqa":
         gen = np.random.default_rng(3)
-        q = (gen.standard_normal((1, w.q_shape[1], 1, w.q_shape[3])) * 0.5).astype(np.float16)
-        kv = [(gen.standard_normal((1, w.kv_shape[1], w.kv_shape[2], w.kv_shape[3])) * 0.5)
-              .astype(np.float16) for _ in range(2)]
-        jobs = [(q, kv[0], kv[1], {"enable_gqa": True})] * max(threads, 8)
-        unit_work = 2 * w.kv_shape[1] * w.kv_shape[2] * w.kv_shape[3] * 2  # K+V bytes per batch row
-    else:
+        q = (gen.standard_normal((1, w.q_shape[1], 1, D)) * 0.5).astype(np.float16)
+        kv = [(gen.standard_normal((1, w.kv_shape[1], w.kv_shape[2], D)) * 0.5).astype(np.float16)
+              for _ in range(2)]
+        jobs = [((q, kv[0], kv[1], {"enable_gqa": True}), 2 * kv[0].nbytes)] * max(threads, 8)
+        what = "batch rows of q (1,32,1,128) vs k/v (1,8,32768,128)"
+    elif name == "fp16_long_causal":
+        if x is None:
+            x = workloads.make(name)
         jobs = []
+        rng = np.random.default_rng(0)
+        for r0 in sorted(rng.integers(0, w.q_shape[2] // 64, size=4 * threads) * 64):
+            h = int(rng.integers(0, w.q_shape[1]))
+            rows = np.arange(r0, r0 + 64)
+            keys = r0 + 64
+            m = np.arange(keys)[None, :] <= rows[:, None]
+            item = (x["q"][0, h, r0:r0 + 64], x["k"][0, h, :keys], x["v"][0, h, :keys],
+                    {"attn_mask": m})
+            jobs.append((item, 4.0 * D * float(np.sum(rows + 1))))
+        what = "64-row query blocks (random heads/offsets) vs their visible keys, forward only"
+    else:
+        if x is None:
+            x = workloads.make(name, batch_rows=slice(0, 1))
         L, S = w.q_shape[2], w.kv_shape[2]
+        unit = 4.0 * L * S * D * (0.5 if w.is_causal else 1.0)
+        jobs = []
         for h in range(w.q_shape[1]):
-            kw = {}
-            if w.is_causal:
-                kw["is_causal"] = True
+            kw = {"is_causal": True} if w.is_causal else {}
             if w.masked:
                 kw["attn_mask"] = x["mask"][0, 0]
-            jobs.append((x["q"][0, h], x["k"][0, h // group], x["v"][0, h // group], kw))
-        unit_work = 4.0 * L * S * w.q_shape[3] * (0.5 if w.is_causal else 1.0)
-    done = 0
+            jobs.append(((x["q"][0, h], x["k"][0, h // group], x["v"][0, h // group], kw), unit))
+        what = "(b,h) slices of the workload"
+    done, work = 0, 0.0
     t0 = time.perf_counter()
     with threadpoolctl.threadpool_limits(limits=1), ThreadPoolExecutor(threads) as ex:
+        pos = 0
         while True:
-            batch = jobs[: max(threads, 1)]
-            list(ex.map(lambda j: fused_sdpa(j[0], j[1], j[2], **j[3]), batch))
+            batch = [jobs[(pos + i) % len(jobs)] for i in range(threads)]
+            pos += threads
+            list(ex.map(lambda j: fused_sdpa(j[0][0], j[0][1], j[0][2], **j[0][3]), batch))
             done += len(batch)
+            work += sum(j[1] for j in batch)
             if time.perf_counter() - t0 > budget_s or done >= 4 * threads:
                 break
     dt = time.perf_counter() - t0
-    rate = done * unit_work / dt
-    if name == "fp16_decode_gqa":
-        return rate / 1e9, threads, f"{done} batch rows of q (1,32,1,128) vs k/v (1,8,32768,128), {dt:.1f}s"
-    return rate / 1e12, threads, f"{done} (b,h) slices of the workload, {dt:.1f}s wall"
+    rate = work / dt / (1e9 if name == "fp16_decode_gqa" else 1e12)
+    return rate, threads, f"{done} {what}, {dt:.1f}s wall"
 
 
 def run_reference(args):
@@ -263,8 +283,11 @@ def workload_config(name, n):
 
 def run_gpu(args):
     rank, local, world, pg = dist_setup(args.gpus)
+    import ctypes
+
     import pa_b200
     from pa_b200 import workloads
+    from pa_b200._lib import check, lib
     from pa_b200.backend import sdpa_device, use_decode_kernel
     from pa_b200.device import DeviceBuffer, Event, Stream
 
@@ -277,23 +300,40 @@ def run_gpu(args):
                              None if mask is None else mask.dtype, w.is_causal, None,
                              w.q_shape[1] // w.kv_shape[1])
     decode = use_decode_kernel(plan)
+    backward = w.backward
     stream = Stream()
     bufs = {}
-    from pa_b200._lib import check, lib
 
-    for key in ("q", "k", "v"):
-        a = np.ascontiguousarray(x[key])
+    def upload(key, arr):
+        a = np.ascontiguousarray(arr)
         bufs[key] = DeviceBuffer(a.nbytes)
         check(lib().pa_memcpy_h2d(bufs[key].ptr, a.ctypes.data, a.nbytes, stream.handle))
+
+    for key in ("q", "k", "v"):
+        upload(key, x[key])
     if mask is not None:
-        m = np.ascontiguousarray(mask).view(np.uint8)
-        bufs["mask"] = DeviceBuffer(m.nbytes)
-        check(lib().pa_memcpy_h2d(bufs["mask"].ptr, m.ctypes.data, m.nbytes, stream.handle))
+        upload("mask", np.ascontiguousarray(mask).view(np.uint8))
     out_bytes = int(np.prod(plan.out_shape)) * plan.cdt.itemsize
     bufs["out"] = DeviceBuffer(out_bytes)
+    if backward:
+        upload("dout", x["dout"])
+        bufs["lse"] = DeviceBuffer(int(np.prod(plan.out_shape[:-1])) * 4)
+        for key in ("dq", "dk", "dv"):
+            bufs[key] = DeviceBuffer(x[key[1]].nbytes)
     stream.synchronize()
+    desc = ctypes.byref(plan.desc)
+    mid = Event() if backward else None
 
-    def step():
+    def step(mark=None):
+        if backward:
+            check(lib().pa_sdpa_fwd(desc, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, None,
+                                    bufs["out"].ptr, bufs["lse"].ptr, stream.handle))
+            if mark is not None:
+                mark.record(stream)
+            check(lib().pa_sdpa_bwd(desc, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr,
+                                    bufs["out"].ptr, bufs["dout"].ptr, bufs["lse"].ptr,
+                                    bufs["dq"].ptr, bufs["dk"].ptr, bufs["dv"].ptr, stream.handle))
+            return
         sdpa_device(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["out"].ptr,
                     mask_ptr=bufs["mask"].ptr if "mask" in bufs else None, stream=stream,
                     decode=decode)
@@ -306,12 +346,13 @@ def run_gpu(args):
     stream.synchronize()
     pa_b200.sync_device_status()
     events = [Event() for _ in range(args.steps + 1)]
+    mids = [Event() for _ in range(args.steps)] if backward else None
     barrier(pg)
     stream.synchronize()
     clocks.mark(0)
     events[0].record(stream)
     for i in range(args.steps):
-        step()
+        step(mids[i] if mids else None)
         events[i + 1].record(stream)
     stream.synchronize()
     clocks.mark(1)
@@ -323,6 +364,7 @@ def run_gpu(args):
     ms = max_over_ranks(pg, ms_local, local)
 
     pk, pk_kind = peaks()
+    extra = {}
     if decode:
         unit = "GB/s"
         work = float(2 * x["k"].nbytes + x["q"].nbytes + out_bytes)
@@ -330,7 +372,24 @@ def run_gpu(args):
         achieved = work / (statistics.mean(per) * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / pk["hbm_gbs"], "traffic": traffic_for(args.workload),
-                "peak_kind": pk_kind, "kernel": "decode_splitkv"}
+                "peak_kind": pk_kind, "kernel": "decode_partial + decode_combine"}
+        launches = 2
+    elif backward:
+        unit = "TFLOP/s"
+        work = w.flops_fwd + w.flops_bwd
+        value = world * work / (ms * 1e-3) / 1e12
+        fwd_ms = statistics.mean(events[i].elapsed_ms(mids[i]) for i in range(args.steps))
+        bwd_ms = statistics.mean(mids[i].elapsed_ms(events[i + 1]) for i in range(args.steps))
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        achieved = w.flops_bwd / (bwd_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic_for(args.workload),
+                "peak_kind": pk_kind + " (sustained: seconds-long step)",
+                "kernel": "backward: bwd_prep + bwd_dkdv + bwd_dq (2.5x forward FLOPs)"}
+        extra = {"fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+                 "fwd_tflops": w.flops_fwd / (fwd_ms * 1e-3) / 1e12,
+                 "bwd_tflops": achieved}
+        launches = 4
     else:
         unit = "TFLOP/s"
         work = w.flops_fwd
@@ -339,48 +398,58 @@ def run_gpu(args):
         roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
                 "traffic": traffic_for(args.workload), "peak_kind": pk_kind + " (burst)",
-                "kernel": "fwd_tc"}
+                "kernel": "fwd_tc" if plan.cdt == np.float16 else "sdpa_exact"}
+        launches = 1
 
     # End to end through the public call on page-locked NumPy inputs.
-    hq = pa_b200.pinned_empty(x["q"].shape, x["q"].dtype)
-    hk = pa_b200.pinned_empty(x["k"].shape, x["k"].dtype)
-    hv = pa_b200.pinned_empty(x["v"].shape, x["v"].dtype)
-    hq[...], hk[...], hv[...] = x["q"], x["k"], x["v"]
+    host = {key: pa_b200.pinned_empty(x[key].shape, x[key].dtype)
+            for key in ("q", "k", "v") + (("dout",) if backward else ())}
+    for key, arr in host.items():
+        arr[...] = x[key]
     kw = {"is_causal": w.is_causal, "enable_gqa": w.enable_gqa}
     if mask is not None:
         kw["attn_mask"] = mask
+
+    def public_call():
+        if backward:
+            return pa_b200.sdpa_backward(host["q"], host["k"], host["v"], host["dout"], **kw)
+        return (pa_b200.scaled_dot_product_attention(host["q"], host["k"], host["v"], **kw),)
+
     for _ in range(max(1, min(args.warmup, 2))):
-        pa_b200.scaled_dot_product_attention(hq, hk, hv, **kw)
+        public_call()
     e2e_steps = max(1, min(args.steps, 5))
     barrier(pg)
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        res = pa_b200.scaled_dot_product_attention(hq, hk, hv, **kw)
+        res = public_call()
     e2e_ms_local = (time.perf_counter() - t0) * 1e3 / e2e_steps
     barrier(pg)
     e2e_ms = max_over_ranks(pg, e2e_ms_local, local)
     e2e_val = world * work / (e2e_ms * 1e-3) / (1e9 if decode else 1e12)
-    h2d = hq.nbytes + hk.nbytes + hv.nbytes + (mask.nbytes if mask is not None else 0)
-    d2h = res.nbytes
+    h2d = sum(a.nbytes for a in host.values()) + (mask.nbytes if mask is not None else 0)
+    d2h = sum(r.nbytes for r in res)
 
     if rank != 0:
+        if pg is not None:
+            pg.destroy_process_group()
         return 0
     line = {
         "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": workload_config(args.workload, world),
+        "vs_baseline": None, "dtype": "f16" if plan.cdt == np.float16 else str(plan.cdt).replace("float", "f"),
+        "data": "synthetic", "config": workload_config(args.workload, world),
         "roofline": roof,
         "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
                 "timing": "host wall clock around the synchronous public call"},
-        "gpu_launches": args.steps * (2 if decode else 1),
+        "gpu_launches": args.steps * launches,
         "clocks": clocks.summary(),
+        **extra,
     }
     if world == 1 and not args.no_cpu:
-        rate, threads, desc = cpu_sample(args.workload)
+        rate, threads, desc_s = cpu_sample(args.workload, x=x if w.backward else None)
         line["cpu_baseline"] = {"value": rate, "unit": unit, "cores": threads, "kind": "port",
-                                "sample": desc + "; oracle port of the fused backend"}
+                                "sample": desc_s + "; oracle port of the fused backend"}
     print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()

@@ -1,0 +1,720 @@
+// Backward (VJP) of the SDPA forward on sm_100a tensor cores.
+//
+// With S = scale * Q K^T, P = softmax(S) (recomputed from the saved lse),
+// dP = dO V^T and dS = P * (dP - rowsum(dO * O)):
+//   dV = P^T dO,   dK = scale * dS^T Q,   dQ = scale * dS K.
+// Three launches, no atomics (results are deterministic):
+//   bwd_prep_kernel   delta = rowsum(dO * O) and lse in log2 units, per row,
+//                     into a row-padded fp32 workspace (rows rounded up to 64).
+//   bwd_dkdv_kernel   CTA = 128 keys of one (batch, KV head). Loops over every
+//                     query head of the grouped-query group and every 64-row
+//                     query block that can see those keys:
+//                       S^T  = K Q^T     (SS, M=128 keys, N=64 rows)
+//                       dP^T = V dO^T    (SS)
+//                       softmax warps: P^T, dS^T -> fp16 into TMEM (aliasing)
+//                       dV  += P^T dO    (TS, B = dO MN-major)
+//                       dK  += dS^T Q    (TS, B = Q MN-major)
+//                     S^T / dP^T are double-buffered so the next block's MMAs
+//                     overlap this block's softmax. dK, dV stay in TMEM until
+//                     the end: grouped-query heads are summed in place.
+//   bwd_dq_kernel     CTA = 128 query rows of one (batch, head). Loops over
+//                     64-key blocks:  S = Q K^T, dP = dO V^T (SS),
+//                     dS -> fp16 into TMEM, dQ += dS K (TS, B = K MN-major).
+// TMEM (512 columns): dkdv S^T[2] 0..127, dP^T[2] 128..255, dV, dK after;
+// dq S[2] 0..127, dP[2] 128..255, dQ at 256.
+// Masking matches the forward: top-left causal (key j visible to row i iff
+// j <= i), keys >= S and rows >= L contribute nothing, and rows whose lse is
+// -inf (fully masked) have P = 0 and so zero gradient.
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pa {
+namespace {
+
+constexpr int kThreadsB = 192;
+constexpr int kRowPad = 64;
+
+struct BwdArgs {
+  void* dk;
+  void* dv;
+  void* dq;
+  const float* lse2;   // [slices_q][Lp], log2 units
+  const float* delta;  // [slices_q][Lp]
+  int* status;
+  int64_t L, S, Lp;
+  int32_t Hq, Hkv, group, blocks;
+  int64_t slices;      // B*Hkv (dkdv) or B*Hq (dq)
+  int32_t causal;
+  float scale_log2, scale;
+};
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if (BF16) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// One warp per row: delta = sum_d dO * O; lse2 = lse * log2(e); padded rows
+// get delta 0 and lse2 -inf.
+template <int D, bool BF16>
+__global__ void bwd_prep_kernel(const void* o, const void* dout, const float* lse, float* delta,
+                                float* lse2, int64_t slices, int64_t L, int64_t Lp) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (r >= slices * Lp) return;
+  const int64_t sl = r / Lp, row = r % Lp;
+  if (row >= L) {
+    if (lane == 0) {
+      delta[r] = 0.f;
+      lse2[r] = -INFINITY;
+    }
+    return;
+  }
+  const int64_t src = (sl * L + row) * D;
+  constexpr int PER = D / 32;  // elements per lane (2 or 4)
+  const uint8_t* ob = static_cast<const uint8_t*>(o) + (src + lane * PER) * 2;
+  const uint8_t* db = static_cast<const uint8_t*>(dout) + (src + lane * PER) * 2;
+  float acc = 0.f;
+  if (PER == 4) {
+    const uint2 a = *reinterpret_cast<const uint2*>(ob);
+    const uint2 b = *reinterpret_cast<const uint2*>(db);
+    const float2 a0 = unpack2<BF16>(a.x), a1 = unpack2<BF16>(a.y);
+    const float2 b0 = unpack2<BF16>(b.x), b1 = unpack2<BF16>(b.y);
+    acc = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
+  } else {
+    const float2 a0 = unpack2<BF16>(*reinterpret_cast<const uint32_t*>(ob));
+    const float2 b0 = unpack2<BF16>(*reinterpret_cast<const uint32_t*>(db));
+    acc = a0.x * b0.x + a0.y * b0.y;
+  }
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    delta[r] = acc;
+    const float l = lse[sl * L + row];
+    lse2[r] = l == -INFINITY ? -INFINITY : l * 1.4426950408889634f;
+  }
+}
+
+// Store 32 fp32 values (scaled) as 16 packed fp16/bf16 words -> 64 bytes.
+template <bool BF16>
+__device__ __forceinline__ void store_row32(uint8_t* dst, const uint32_t (&rr)[32], float mul) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t)
+    pk[t] = pack2(__uint_as_float(rr[2 * t]) * mul, __uint_as_float(rr[2 * t + 1]) * mul, BF16);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) d4[t] = make_uint4(pk[4 * t], pk[4 * t + 1], pk[4 * t + 2], pk[4 * t + 3]);
+}
+
+// ------------------------------------------------------------------ dK / dV
+
+template <int D>
+struct DkdvCfg {
+  static constexpr int BQ = 64, BK = 128;
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kKVBytes = BK * D * 2;
+  static constexpr int kQBytes = BQ * D * 2;
+  static constexpr int kStages = 3;
+  static constexpr int kStageBytes = ((2 * kQBytes + 2 * BQ * 4) + 1023) / 1024 * 1024;
+  static constexpr int kKOff = 0, kVOff = kKVBytes, kStageOff = 2 * kKVBytes;
+  static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
+  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
+  static constexpr uint32_t kColS = 0, kColP = 128, kColV = 256, kColK = 256 + D;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreadsB, 1)
+    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                    const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                    const BwdArgs a) {
+  using C = DkdvCfg<D>;
+  constexpr int BQ = C::BQ, BK = C::BK;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sK = smem + C::kKOff;
+  uint8_t* sV = smem + C::kVOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = qd_full + C::kStages;
+  uint64_t* sdp_full = qd_empty + C::kStages;  // [2]
+  uint64_t* ds_ready = sdp_full + 2;            // [2]
+  uint64_t* acc_done = ds_ready + 2;
+  uint64_t* mma_done = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kv_blk = static_cast<int>(blockIdx.x / a.slices);  // low blocks (most work) first
+  const int64_t pair = blockIdx.x % a.slices;                  // b * Hkv + kvh
+  const int64_t n0 = static_cast<int64_t>(kv_blk) * BK;
+  const int64_t b = pair / a.Hkv;
+  const int kvh = static_cast<int>(pair % a.Hkv);
+  const int nqb = static_cast<int>((a.L + BQ - 1) / BQ);
+  const int qb0 = a.causal ? static_cast<int>(n0 / BQ) : 0;
+  const int per_head = nqb > qb0 ? nqb - qb0 : 0;
+  const int n = per_head * a.group;
+  auto stage_ptr = [&](int st) { return smem + C::kStageOff + st * C::kStageBytes; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(qd_full + s, 1);
+      mbar_init(qd_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(sdp_full + s, 1);
+      mbar_init(ds_ready + s, 128);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tdo);
+      mbar_expect_tx(kv_full, 2 * C::kKVBytes);
+      for (int bx = 0; bx < C::kBoxes; ++bx) {
+        tma_load_3d(sK + bx * (BK * 128), &tk, kv_full, bx * 64, static_cast<int32_t>(n0), static_cast<int32_t>(pair));
+        tma_load_3d(sV + bx * (BK * 128), &tv, kv_full, bx * 64, static_cast<int32_t>(n0), static_cast<int32_t>(pair));
+      }
+      int last[C::kStages];
+#pragma unroll
+      for (int s = 0; s < C::kStages; ++s) last[s] = -1;
+      for (int i = 0; i < n; ++i) {
+        const int st = i % C::kStages;
+        if (!mbar_wait(qd_empty + st, ((i / C::kStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
+        const int h = i / per_head;
+        const int64_t q0 = static_cast<int64_t>(qb0 + i % per_head) * BQ;
+        const int64_t zq = b * a.Hq + static_cast<int64_t>(kvh) * a.group + h;
+        uint8_t* sp = stage_ptr(st);
+        mbar_expect_tx(qd_full + st, 2 * C::kQBytes + 2 * BQ * 4);
+        for (int bx = 0; bx < C::kBoxes; ++bx) {
+          tma_load_3d(sp + bx * (BQ * 128), &tq, qd_full + st, bx * 64, static_cast<int32_t>(q0), static_cast<int32_t>(zq));
+          tma_load_3d(sp + C::kQBytes + bx * (BQ * 128), &tdo, qd_full + st, bx * 64, static_cast<int32_t>(q0),
+                      static_cast<int32_t>(zq));
+        }
+        bulk_load(sp + 2 * C::kQBytes, a.lse2 + zq * a.Lp + q0, BQ * 4, qd_full + st);
+        bulk_load(sp + 2 * C::kQBytes + BQ * 4, a.delta + zq * a.Lp + q0, BQ * 4, qd_full + st);
+        last[st] = i;
+      }
+      mbar_drain(kv_full, 0);
+#pragma unroll
+      for (int s = 0; s < C::kStages; ++s)
+        if (last[s] >= 0) mbar_drain(qd_full + s, (last[s] / C::kStages) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      constexpr uint32_t idS = idesc_f16(128, BQ, false, false, BF16);
+      constexpr uint32_t idA = idesc_f16(128, D, false, true, BF16);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      bool ok = mbar_wait(kv_full, 0, a.status, kStatusTimeoutLoad, abort_flag);
+      auto issue_sdp = [&](int i) -> bool {
+        const int st = i % C::kStages;
+        if (!mbar_wait(qd_full + st, (i / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t sb = i & 1;
+        const uint32_t q_addr = smem_u32(stage_ptr(st)), do_addr = q_addr + C::kQBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t bx = kk / 4, sub = (kk % 4) * 32;
+          umma_ss(tmem + C::kColS + sb * 64, sdesc_sw128(k_addr + bx * (BK * 128) + sub, 16, 1024),
+                  sdesc_sw128(q_addr + bx * (BQ * 128) + sub, 16, 1024), idS, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t bx = kk / 4, sub = (kk % 4) * 32;
+          umma_ss(tmem + C::kColP + sb * 64, sdesc_sw128(v_addr + bx * (BK * 128) + sub, 16, 1024),
+                  sdesc_sw128(do_addr + bx * (BQ * 128) + sub, 16, 1024), idS, kk > 0);
+        }
+        tc_commit(sdp_full + sb);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int i = 0; ok && i < n; ++i) {
+        if (i + 1 < n && !issue_sdp(i + 1)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sb = i & 1;
+        if (!mbar_wait(ds_ready + sb, (i >> 1) & 1, a.status, kStatusTimeoutSoftmax, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int st = i % C::kStages;
+        const uint32_t q_addr = smem_u32(stage_ptr(st)), do_addr = q_addr + C::kQBytes;
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          umma_ts(tmem + C::kColV, tmem + C::kColS + sb * 64 + kk * 8,
+                  sdesc_sw128(do_addr + kk * 2048, BQ * 128, 1024), idA, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          umma_ts(tmem + C::kColK, tmem + C::kColP + sb * 64 + kk * 8,
+                  sdesc_sw128(q_addr + kk * 2048, BQ * 128, 1024), idA, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(qd_empty + st);
+      }
+      tc_commit(acc_done);
+      tc_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int64_t key = n0 + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      const uint32_t sb = i & 1;
+      const int st = i % C::kStages;
+      ok = mbar_wait(sdp_full + sb, (i >> 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
+      ok = ok && mbar_wait(qd_full + st, (i / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const float* l2 = reinterpret_cast<const float*>(stage_ptr(st) + 2 * C::kQBytes);
+      const float* dl = l2 + BQ;
+      const int64_t q0 = static_cast<int64_t>(qb0 + i % per_head) * BQ;
+      uint32_t pk[32], dk[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sr[32], pr[32];
+        tmem_ld32(lane_base + C::kColS + sb * 64 + half * 32, sr);
+        tmem_ld32(lane_base + C::kColP + sb * 64 + half * 32, pr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          float p2[2], d2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int c = half * 32 + 2 * t + u;
+            const int64_t qrow = q0 + c;
+            const float lz = l2[c];
+            const bool vis = qrow < a.L && (!a.causal || key <= qrow) && lz != -INFINITY;
+            const float p = vis ? ex2(__uint_as_float(sr[2 * t + u]) * a.scale_log2 - lz) : 0.f;
+            p2[u] = p;
+            d2[u] = vis ? p * (__uint_as_float(pr[2 * t + u]) - dl[c]) : 0.f;
+          }
+          pk[half * 16 + t] = pack2(p2[0], p2[1], BF16);
+          dk[half * 16 + t] = pack2(d2[0], d2[1], BF16);
+        }
+      }
+      tmem_st32(lane_base + C::kColS + sb * 64, pk);
+      tmem_st32(lane_base + C::kColP + sb * 64, dk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(ds_ready + sb);
+    }
+    if (ok && n > 0) {
+      ok = mbar_wait(acc_done, 0, a.status, kStatusTimeoutMma, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const bool row_ok = key < a.S;
+      uint8_t* dvrow = static_cast<uint8_t*>(a.dv) + ((pair * a.S + key) * D) * 2;
+      uint8_t* dkrow = static_cast<uint8_t*>(a.dk) + ((pair * a.S + key) * D) * 2;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t rv[32], rk[32];
+        if (n > 0) {
+          tmem_ld32(lane_base + C::kColV + c * 32, rv);
+          tmem_ld32(lane_base + C::kColK + c * 32, rk);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) rv[t] = rk[t] = 0u;
+        }
+        if (row_ok) {
+          store_row32<BF16>(dvrow + c * 64, rv, 1.f);
+          store_row32<BF16>(dkrow + c * 64, rk, a.scale);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------- dQ
+
+template <int D>
+struct DqCfg {
+  static constexpr int BQ = 128, BK = 64;
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kQBytes = BQ * D * 2;
+  static constexpr int kKBytes = BK * D * 2;
+  static constexpr int kStages = 3;
+  static constexpr int kQOff = 0, kDOOff = kQBytes, kStageOff = 2 * kQBytes;
+  static constexpr int kStageBytes = 2 * kKBytes;
+  static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
+  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
+  static constexpr uint32_t kColS = 0, kColP = 128, kColQ = 256;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreadsB, 1)
+    bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                  const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                  const BwdArgs a) {
+  using C = DqCfg<D>;
+  constexpr int BQ = C::BQ, BK = C::BK;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sQ = smem + C::kQOff;
+  uint8_t* sDO = smem + C::kDOOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + C::kStages;
+  uint64_t* sdp_full = kv_empty + C::kStages;
+  uint64_t* ds_ready = sdp_full + 2;
+  uint64_t* acc_done = ds_ready + 2;
+  uint64_t* mma_done = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_blk = a.blocks - 1 - static_cast<int>(blockIdx.x / a.slices);  // heaviest first
+  const int64_t zq = blockIdx.x % a.slices;                                   // b * Hq + h
+  const int64_t m0 = static_cast<int64_t>(m_blk) * BQ;
+  const int64_t zkv = (zq / a.Hq) * a.Hkv + (zq % a.Hq) / a.group;
+  int64_t kv_end = a.S;
+  if (a.causal) {
+    const int64_t last = (m0 + BQ < a.L ? m0 + BQ : a.L);
+    kv_end = last < a.S ? last : a.S;
+  }
+  const int n = static_cast<int>((kv_end + BK - 1) / BK);
+  auto stage_ptr = [&](int st) { return smem + C::kStageOff + st * C::kStageBytes; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(sdp_full + s, 1);
+      mbar_init(ds_ready + s, 128);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && n > 0) {
+      mbar_expect_tx(q_full, 2 * C::kQBytes);
+      for (int bx = 0; bx < C::kBoxes; ++bx) {
+        tma_load_3d(sQ + bx * (BQ * 128), &tq, q_full, bx * 64, static_cast<int32_t>(m0), static_cast<int32_t>(zq));
+        tma_load_3d(sDO + bx * (BQ * 128), &tdo, q_full, bx * 64, static_cast<int32_t>(m0), static_cast<int32_t>(zq));
+      }
+      int last[C::kStages];
+#pragma unroll
+      for (int s = 0; s < C::kStages; ++s) last[s] = -1;
+      for (int j = 0; j < n; ++j) {
+        const int st = j % C::kStages;
+        if (!mbar_wait(kv_empty + st, ((j / C::kStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
+        uint8_t* sp = stage_ptr(st);
+        mbar_expect_tx(kv_full + st, C::kStageBytes);
+        for (int bx = 0; bx < C::kBoxes; ++bx) {
+          tma_load_3d(sp + bx * (BK * 128), &tk, kv_full + st, bx * 64, j * BK, static_cast<int32_t>(zkv));
+          tma_load_3d(sp + C::kKBytes + bx * (BK * 128), &tv, kv_full + st, bx * 64, j * BK,
+                      static_cast<int32_t>(zkv));
+        }
+        last[st] = j;
+      }
+      mbar_drain(q_full, 0);
+#pragma unroll
+      for (int s = 0; s < C::kStages; ++s)
+        if (last[s] >= 0) mbar_drain(kv_full + s, (last[s] / C::kStages) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      constexpr uint32_t idS = idesc_f16(128, BK, false, false, BF16);
+      constexpr uint32_t idQ = idesc_f16(128, D, false, true, BF16);
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      bool ok = mbar_wait(q_full, 0, a.status, kStatusTimeoutLoad, abort_flag);
+      auto issue_sdp = [&](int j) -> bool {
+        const int st = j % C::kStages;
+        if (!mbar_wait(kv_full + st, (j / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t sb = j & 1;
+        const uint32_t k_addr = smem_u32(stage_ptr(st)), v_addr = k_addr + C::kKBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t bx = kk / 4, sub = (kk % 4) * 32;
+          umma_ss(tmem + C::kColS + sb * 64, sdesc_sw128(q_addr + bx * (BQ * 128) + sub, 16, 1024),
+                  sdesc_sw128(k_addr + bx * (BK * 128) + sub, 16, 1024), idS, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t bx = kk / 4, sub = (kk % 4) * 32;
+          umma_ss(tmem + C::kColP + sb * 64, sdesc_sw128(do_addr + bx * (BQ * 128) + sub, 16, 1024),
+                  sdesc_sw128(v_addr + bx * (BK * 128) + sub, 16, 1024), idS, kk > 0);
+        }
+        tc_commit(sdp_full + sb);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n && !issue_sdp(j + 1)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sb = j & 1;
+        if (!mbar_wait(ds_ready + sb, (j >> 1) & 1, a.status, kStatusTimeoutSoftmax, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int st = j % C::kStages;
+        const uint32_t k_addr = smem_u32(stage_ptr(st));
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_ts(tmem + C::kColQ, tmem + C::kColP + sb * 64 + kk * 8,
+                  sdesc_sw128(k_addr + kk * 2048, BK * 128, 1024), idQ, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(kv_empty + st);
+      }
+      tc_commit(acc_done);
+      tc_commit(mma_done);
+      mbar_drain(mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int64_t row = m0 + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const float lz = a.lse2[zq * a.Lp + row];  // padded rows hold -inf
+    const float dlt = a.delta[zq * a.Lp + row];
+    const bool row_live = row < a.L && lz != -INFINITY;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const uint32_t sb = j & 1;
+      ok = mbar_wait(sdp_full + sb, (j >> 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int64_t k0 = static_cast<int64_t>(j) * BK;
+      const int64_t vis = a.causal ? (row + 1 < a.S ? row + 1 : a.S) : a.S;
+      uint32_t dk[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sr[32], pr[32];
+        tmem_ld32(lane_base + C::kColS + sb * 64 + half * 32, sr);
+        tmem_ld32(lane_base + C::kColP + sb * 64 + half * 32, pr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          float d2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int c = half * 32 + 2 * t + u;
+            const bool vis_c = row_live && (k0 + c) < vis;
+            const float p = vis_c ? ex2(__uint_as_float(sr[2 * t + u]) * a.scale_log2 - lz) : 0.f;
+            d2[u] = vis_c ? p * (__uint_as_float(pr[2 * t + u]) - dlt) : 0.f;
+          }
+          dk[half * 16 + t] = pack2(d2[0], d2[1], BF16);
+        }
+      }
+      tmem_st32(lane_base + C::kColP + sb * 64, dk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(ds_ready + sb);
+    }
+    if (ok && n > 0) {
+      ok = mbar_wait(acc_done, 0, a.status, kStatusTimeoutMma, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      uint8_t* dqrow = static_cast<uint8_t*>(a.dq) + ((zq * a.L + row) * D) * 2;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t rq[32];
+        if (n > 0) {
+          tmem_ld32(lane_base + C::kColQ + c * 32, rq);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) rq[t] = 0u;
+        }
+        if (row < a.L) store_row32<BF16>(dqrow + c * 64, rq, a.scale);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D, bool BF16>
+pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv, const void* q,
+                        const void* k, const void* v, const void* o, const void* dout,
+                        const float* lse, void* dq, void* dk, void* dv, cudaStream_t st) {
+  const int64_t L = d.L, S = d.S;
+  const int64_t Lp = (L + kRowPad - 1) / kRowPad * kRowPad;
+  const int64_t nkv = (n / H) * Hkv;
+  float* ws = nullptr;
+  const size_t ws_floats = 2 * static_cast<size_t>(n * Lp) + 2 * kRowPad;
+  PA_TRY(scratch_alloc(reinterpret_cast<void**>(&ws), ws_floats * sizeof(float), st));
+  float* delta = ws;
+  float* lse2 = ws + n * Lp + kRowPad;
+  pa_status rc = PA_OK;
+  do {
+    const int64_t rows = n * Lp;
+    const int64_t threads = rows * 32;
+    bwd_prep_kernel<D, BF16><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
+        o, dout, lse, delta, lse2, n, L, Lp);
+    if (cudaGetLastError() != cudaSuccess) {
+      rc = fail(PA_ERR_CUDA, "bwd_prep launch failed");
+      break;
+    }
+    const CUtensorMapDataType tdt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t rowb = D * 2;
+    CUtensorMap tq64, tdo64, tk128, tv128, tq128, tdo128, tk64, tv64;
+    rc = encode_tma_3d(&tq64, tdt, q, D, L, n, rowb, rowb * L, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == PA_OK) rc = encode_tma_3d(&tdo64, tdt, dout, D, L, n, rowb, rowb * L, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == PA_OK) rc = encode_tma_3d(&tk128, tdt, k, D, S, nkv, rowb, rowb * S, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == PA_OK) rc = encode_tma_3d(&tv128, tdt, v, D, S, nkv, rowb, rowb * S, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == PA_OK) rc = encode_tma_3d(&tq128, tdt, q, D, L, n, rowb, rowb * L, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == PA_OK) rc = encode_tma_3d(&tdo128, tdt, dout, D, L, n, rowb, rowb * L, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == PA_OK) rc = encode_tma_3d(&tk64, tdt, k, D, S, nkv, rowb, rowb * S, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == PA_OK) rc = encode_tma_3d(&tv64, tdt, v, D, S, nkv, rowb, rowb * S, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != PA_OK) break;
+    BwdArgs a{};
+    a.dk = dk;
+    a.dv = dv;
+    a.dq = dq;
+    a.lse2 = lse2;
+    a.delta = delta;
+    a.status = device_status_word();
+    if (!a.status) {
+      rc = fail(PA_ERR_CUDA, "device status word unavailable");
+      break;
+    }
+    a.L = L;
+    a.S = S;
+    a.Lp = Lp;
+    a.Hq = static_cast<int32_t>(H);
+    a.Hkv = static_cast<int32_t>(Hkv);
+    a.group = static_cast<int32_t>(H / Hkv);
+    a.causal = d.is_causal;
+    a.scale_log2 = static_cast<float>(d.scale * 1.4426950408889634);
+    a.scale = static_cast<float>(d.scale);
+    {
+      using C = DkdvCfg<D>;
+      a.slices = nkv;
+      a.blocks = static_cast<int32_t>((S + C::BK - 1) / C::BK);
+      const int64_t grid = nkv * a.blocks;
+      auto kern = bwd_dkdv_kernel<D, BF16>;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess) {
+        rc = fail(PA_ERR_CUDA, "bwd_dkdv: shared memory attribute");
+        break;
+      }
+      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tq64, tdo64, tk128, tv128, a);
+      if (cudaGetLastError() != cudaSuccess) {
+        rc = fail(PA_ERR_CUDA, "bwd_dkdv launch failed");
+        break;
+      }
+    }
+    {
+      using C = DqCfg<D>;
+      a.slices = n;
+      a.blocks = static_cast<int32_t>((L + C::BQ - 1) / C::BQ);
+      const int64_t grid = n * a.blocks;
+      auto kern = bwd_dq_kernel<D, BF16>;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess) {
+        rc = fail(PA_ERR_CUDA, "bwd_dq: shared memory attribute");
+        break;
+      }
+      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tq128, tdo128, tk64, tv64, a);
+      if (cudaGetLastError() != cudaSuccess) {
+        rc = fail(PA_ERR_CUDA, "bwd_dq launch failed");
+        break;
+      }
+    }
+  } while (false);
+  scratch_free(ws, st);
+  return rc;
+}
+
+}  // namespace
+}  // namespace pa
+
+using namespace pa;
+
+extern "C" pa_status pa_sdpa_bwd(const pa_sdpa_desc* desc, const void* q, const void* k,
+                                 const void* v, const void* out, const void* dout,
+                                 const float* lse, void* dq, void* dk, void* dv, void* stream) {
+  clear_error();
+  PA_TRY(check_desc(desc));
+  const pa_sdpa_desc& d = *desc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (d.mask_kind != PA_MASK_NONE)
+    return fail(PA_ERR_UNSUPPORTED, "pa_sdpa_bwd: attn_mask is not supported by the backward yet");
+  std::string why;
+  if (!fwd_tc_eligible(d, &why))
+    return fail(PA_ERR_UNSUPPORTED, "pa_sdpa_bwd needs dense fp16/bf16 (B, H, L, D) with D in {64, 128}: " + why);
+  int64_t n, H, Hkv;
+  dense_bhsd(d, &n, &H, &Hkv);
+  if (n == 0 || (d.L == 0 && d.S == 0)) return PA_OK;
+  if (d.S == 0 || d.L == 0) {
+    // No keys: every gradient is zero; no rows: dK and dV are zero.
+    const size_t es = 2;
+    if (d.L) PA_CUDA(cudaMemsetAsync(dq, 0, static_cast<size_t>(n * d.L * d.E) * es, st));
+    if (d.S) {
+      const size_t kv = static_cast<size_t>((n / H) * Hkv * d.S * d.E) * es;
+      PA_CUDA(cudaMemsetAsync(dk, 0, kv, st));
+      PA_CUDA(cudaMemsetAsync(dv, 0, kv, st));
+    }
+    return PA_OK;
+  }
+  const bool bf16 = d.dtype == PA_BF16;
+  if (d.E == 128)
+    return bf16 ? launch_bwd_tc<128, true>(d, n, H, Hkv, q, k, v, out, dout, lse, dq, dk, dv, st)
+                : launch_bwd_tc<128, false>(d, n, H, Hkv, q, k, v, out, dout, lse, dq, dk, dv, st);
+  return bf16 ? launch_bwd_tc<64, true>(d, n, H, Hkv, q, k, v, out, dout, lse, dq, dk, dv, st)
+              : launch_bwd_tc<64, false>(d, n, H, Hkv, q, k, v, out, dout, lse, dq, dk, dv, st);
+}

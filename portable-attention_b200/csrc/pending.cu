@@ -4,10 +4,6 @@
 using namespace pa;
 
 extern "C" {
-pa_status pa_sdpa_bwd(const pa_sdpa_desc*, const void*, const void*, const void*, const void*,
-                      const void*, const float*, void*, void*, void*, void*) {
-  return fail(PA_ERR_UNSUPPORTED, "pa_sdpa_bwd is not built yet");
-}
 pa_status pa_comm_unique_id(uint8_t*) { return fail(PA_ERR_UNSUPPORTED, "ring not built yet"); }
 pa_status pa_comm_init(pa_comm**, const uint8_t*, int32_t, int32_t) {
   return fail(PA_ERR_UNSUPPORTED, "ring not built yet");
