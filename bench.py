@@ -293,6 +293,8 @@ def run_gpu(args):
 
     pa_b200.set_device(local)
     w = workloads.WORKLOADS[args.workload]
+    if w.backward and world > 1:
+        return run_ring(args, rank, local, world, pg)
     x = workloads.make(args.workload)
     mask = x.get("mask")
     plan = pa_b200.plan_call(x["q"].shape, x["k"].shape, x["v"].shape, x["q"].dtype, x["k"].dtype,
@@ -451,6 +453,120 @@ def run_gpu(args):
         line["cpu_baseline"] = {"value": rate, "unit": unit, "cores": threads, "kind": "port",
                                 "sample": desc_s + "; oracle port of the fused backend"}
     print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+def run_ring(args, rank, local, world, pg):
+    """Long-context causal fwd+bwd, sequence-sharded over ``world`` GPUs (ring attention).
+
+    Every rank keeps its zig-zag shard of the one global problem (strong
+    scaling: total work is fixed); K/V move between GPUs with NCCL inside
+    ``pa_ring_fwd`` / ``pa_ring_bwd``. ``value`` = the global problem's fwd+bwd
+    FLOPs over the max-over-ranks step time.
+    """
+    import ctypes
+
+    import pa_b200
+    from pa_b200 import workloads
+    from pa_b200._lib import check, lib
+    from pa_b200.device import DeviceBuffer, Event, Stream
+    from pa_b200.ring import RingComm, shard
+
+    w = workloads.WORKLOADS[args.workload]
+    x = workloads.make(args.workload)
+    sh = {key: np.ascontiguousarray(shard(x[key], world, rank)) for key in ("q", "k", "v", "dout")}
+    del x
+    plan = pa_b200.plan_call(sh["q"].shape, sh["k"].shape, sh["v"].shape, sh["q"].dtype, sh["k"].dtype,
+                             sh["v"].dtype, is_causal=True)
+    comm = RingComm.from_process_group()
+    stream = Stream()
+    bufs = {key: DeviceBuffer(arr.nbytes) for key, arr in sh.items()}
+    for key, arr in sh.items():
+        check(lib().pa_memcpy_h2d(bufs[key].ptr, arr.ctypes.data, arr.nbytes, stream.handle))
+    for key in ("out", "dq", "dk", "dv"):
+        bufs[key] = DeviceBuffer(sh["q"].nbytes)
+    bufs["lse"] = DeviceBuffer(int(np.prod(sh["q"].shape[:-1])) * 4)
+    stream.synchronize()
+
+    def step(mark=None):
+        comm.forward(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["out"].ptr,
+                     bufs["lse"].ptr, stream)
+        if mark is not None:
+            mark.record(stream)
+        comm.backward(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["out"].ptr,
+                      bufs["dout"].ptr, bufs["lse"].ptr, bufs["dq"].ptr, bufs["dk"].ptr,
+                      bufs["dv"].ptr, stream)
+
+    out_dir = ROOT / "gpurun_out"
+    out_dir.mkdir(exist_ok=True)
+    clocks = ClockSampler(local, out_dir / f"clocks_rank{rank}.csv").start()
+    for _ in range(args.warmup):
+        step()
+    comm.wait(stream, timeout_ms=300000)
+    pa_b200.sync_device_status()
+    events = [Event() for _ in range(args.steps + 1)]
+    mids = [Event() for _ in range(args.steps)]
+    barrier(pg)
+    clocks.mark(0)
+    events[0].record(stream)
+    for i in range(args.steps):
+        step(mids[i])
+        events[i + 1].record(stream)
+    comm.wait(stream, timeout_ms=300000)
+    clocks.mark(1)
+    clocks.stop()
+    barrier(pg)
+    ms = max_over_ranks(pg, events[0].elapsed_ms(events[-1]) / args.steps, local)
+    fwd_ms = max_over_ranks(pg, statistics.mean(events[i].elapsed_ms(mids[i]) for i in range(args.steps)), local)
+    bwd_ms = max_over_ranks(pg, statistics.mean(mids[i].elapsed_ms(events[i + 1]) for i in range(args.steps)), local)
+    work = w.flops_fwd + w.flops_bwd
+    value = work / (ms * 1e-3) / 1e12
+    pk, pk_kind = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    per_gpu = value / world
+    roof = {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+            "frac": per_gpu / peak, "traffic": None, "peak_kind": pk_kind + " (sustained)",
+            "kernel": "ring step (fwd_tc + bwd kernels per chunk pair, NCCL send/recv overlapped)"}
+
+    # End to end: pinned host shards in, gradients out, around the public ring calls.
+    host = {key: pa_b200.pinned_empty(arr.shape, arr.dtype) for key, arr in sh.items()}
+    for key in host:
+        host[key][...] = sh[key]
+    res = {key: pa_b200.pinned_empty(sh["q"].shape, sh["q"].dtype) for key in ("dq", "dk", "dv")}
+    barrier(pg)
+    t0 = time.perf_counter()
+    e2e_steps = max(1, min(args.steps, 3))
+    for _ in range(e2e_steps):
+        for key, arr in host.items():
+            check(lib().pa_memcpy_h2d(bufs[key].ptr, arr.ctypes.data, arr.nbytes, stream.handle))
+        step()
+        for key, arr in res.items():
+            check(lib().pa_memcpy_d2h(arr.ctypes.data, bufs[key].ptr, arr.nbytes, stream.handle))
+        comm.wait(stream, timeout_ms=300000)
+    e2e_ms = max_over_ranks(pg, (time.perf_counter() - t0) * 1e3 / e2e_steps, local)
+    h2d = sum(a.nbytes for a in host.values())
+    d2h = sum(a.nbytes for a in res.values())
+    summary = clocks.summary()
+    comm.close()
+    if rank == 0:
+        cfg = workload_config(args.workload, world)
+        cfg["global_batch"] = w.q_shape[0]
+        cfg["parallelism"] = f"ring (zig-zag sequence shards) x{world}"
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic", "config": cfg, "roofline": roof,
+            "e2e": {"value": work / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(h2d) * world, "d2h_bytes_per_step": int(d2h) * world,
+                    "ms_per_step": e2e_ms, "timing": "host wall clock, pinned shards, max over ranks"},
+            # per rank per step: fwd 2 per chunk pair + 6 fills/stores, bwd 6 per pair + 8
+            "gpu_launches": args.steps * (8 * (2 * world + 1) + 14), "clocks": summary,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        }
+        print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()
     return 0

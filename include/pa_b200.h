@@ -205,6 +205,11 @@ typedef struct pa_comm pa_comm;
 pa_status pa_comm_unique_id(uint8_t id[128]);
 pa_status pa_comm_init(pa_comm** comm, const uint8_t id[128], int32_t nranks, int32_t rank);
 pa_status pa_comm_destroy(pa_comm* comm);
+/* Wait (host side, bounded) until `stream` and the communicator's side stream
+ * are idle. On an NCCL asynchronous error or when `timeout_ms` (>= 0) passes,
+ * the communicator is aborted and PA_ERR_NCCL / PA_ERR_TIMEOUT is returned, so
+ * a dead peer ends in an error instead of a hang. */
+pa_status pa_comm_wait(pa_comm* comm, void* stream, int32_t timeout_ms);
 
 /*
  * Ring (context-parallel) causal attention over `comm`. Each rank holds its

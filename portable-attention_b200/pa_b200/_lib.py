@@ -111,6 +111,7 @@ SIGNATURES = {
     "pa_comm_unique_id": [ctypes.c_char_p],
     "pa_comm_init": [ctypes.POINTER(_P), ctypes.c_char_p, _I32, _I32],
     "pa_comm_destroy": [_P],
+    "pa_comm_wait": [_P, _P, _I32],
     "pa_ring_fwd": [_P, _DESC, _P, _P, _P, _P, _P, _P],
     "pa_ring_bwd": [_P, _DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
 }
@@ -125,6 +126,27 @@ def library_path() -> Path:
     return Path(env) if env else Path(__file__).resolve().parent / "libpa_b200.so"
 
 
+def _prefer_python_nccl() -> None:
+    """Point the library's lazy NCCL load at the pip ``nvidia-nccl`` build when present.
+
+    Frameworks in the same process (PyTorch) load that build; using the same
+    file avoids two different ``libnccl.so.2`` in one process.
+    """
+    if os.environ.get("PA_B200_NCCL"):
+        return
+    try:
+        import importlib.util
+
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        cand = Path(base) / "lib" / "libnccl.so.2"
+        if cand.exists():
+            os.environ["PA_B200_NCCL"] = str(cand)
+            return
+
+
 def lib() -> ctypes.CDLL:
     """Load (once) and return the native library, with every signature declared."""
     global _handle
@@ -137,6 +159,7 @@ def lib() -> ctypes.CDLL:
                 raise LibraryError(
                     f"libpa_b200.so not found at {path}; build it with "
                     "`python portable-attention_b200/build.py`")
+            _prefer_python_nccl()
             try:
                 h = ctypes.CDLL(str(path))
             except OSError as exc:
