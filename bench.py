@@ -401,7 +401,8 @@ def run_gpu(args):
                 "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
                 "traffic": traffic_for(args.workload), "peak_kind": pk_kind + " (burst)",
                 "kernel": "fwd_tc" if plan.cdt == np.float16 else "sdpa_exact"}
-        launches = 1
+        # a boolean mask adds the tile-classification pre-pass
+        launches = 2 if (mask is not None and mask.dtype == np.bool_) else 1
 
     # End to end through the public call on page-locked NumPy inputs.
     host = {key: pa_b200.pinned_empty(x[key].shape, x[key].dtype)

@@ -1,25 +1,35 @@
 // Tensor-core SDPA forward for sm_100a: TMA-fed tiles, tcgen05.mma into
 // TMEM, online softmax in fp32 with one query row per thread.
 //
-// CTA = one 128-row query tile of one (batch, head). 192 threads:
-//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys into a ring
-//               of shared-memory stages (128-byte swizzle, 64-column boxes).
-//   warp 1      owns TMEM (512 columns) and issues the MMAs from one lane:
-//                 S_j  = Q K_j^T        (SS form, M=128 N=128 K=D) -> S[j%2]
-//                 O   += P_j V_j        (TS form: P_j read from TMEM) -> O
-//   warps 2..5  softmax: thread <-> TMEM lane <-> query row. Loads S_j,
-//               applies scale / causal / mask / key-bound, keeps a running
-//               max m and sum l, writes P_j = 2^(x - m) as fp16/bf16 into the
-//               first 64 columns of S[j%2] (aliasing S_j), rescales O only
-//               when its row max grows by more than 2^8, and finally writes
-//               O / l and the natural-log lse.
-// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).
+// CTA = two 128-row query tiles (256 rows) of one (batch, head), 320 threads:
+//   warps 0-3   softmax of query tile 0; warps 4-7 softmax of tile 1. Thread
+//               <-> TMEM lane <-> query row (warp w reaches lanes 32*(w%4)..).
+//   warp 8      TMA producer: both Q tiles once, then 128-key K/V tiles into a
+//               ring of shared-memory stages (128-byte swizzle, 64-col boxes).
+//   warp 9      owns TMEM (512 columns) and issues the MMAs from one lane:
+//                 S_t = Q_t K^T  (SS form, M=128 N=128 K=D)      -> S[t]
+//                 O_t += P_t V   (TS form, P_t read from TMEM)    -> O[t]
+//               in the order S0(i), PV1(i-1), S1(i), PV0(i), so one tile's
+//               softmax overlaps the other tile's tensor-core work.
+// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D), O1 after.
 //
-// Semantics follow src/portable_attention/reference.py:139-162: top-left
-// causal alignment (key j visible to row i iff j <= i), boolean keep-masks,
-// additive masks, and exact-zero output for fully-masked rows (l == 0).
-// Every wait is bounded; a wait that gives up records a status code and the
-// CTA drains its in-flight copies and MMAs before freeing TMEM.
+// Softmax per key tile: the row max is taken on raw scores (scale > 0), each
+// probability costs one FFMA and one ex2, partial max/sum chains are split
+// eight ways for ILP, and P is packed to fp16/bf16 into the first 64 columns
+// of its S buffer (aliasing S). The running max moves only when it grows by
+// more than 2^8 (log2 units), so O is rescaled rarely. Fully-masked rows keep
+// l = 0 and produce exact zeros and lse = -inf.
+//
+// Key tiles are classified per query tile: dead (causally invisible, or a
+// boolean-mask tile with no kept element: no MMA, no softmax), full (no
+// per-element work) or partial (diagonal, ragged key edge, mixed mask tile:
+// per-element masking, 16-byte vector mask loads when the mask row allows).
+// Boolean-mask tile classes come from a pre-pass over the mask.
+//
+// Semantics follow src/portable_attention/reference.py:139-162 (top-left
+// causal, keep-masks, additive masks, dead rows exactly zero). Every wait is
+// bounded; a wait that gives up records a status code and the CTA drains its
+// copies and MMAs before freeing TMEM.
 #include <math.h>
 
 #include "common.cuh"
@@ -30,52 +40,107 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int kThreads = 192;
+constexpr int kTiles = 2;
+constexpr int kSoftWarps = 4 * kTiles;
+constexpr int kProducerWarp = kSoftWarps;
+constexpr int kMmaWarp = kSoftWarps + 1;
+constexpr int kThreads = 32 * (kSoftWarps + 2);
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
-constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-// Running max moves only when the block max exceeds it by more than this
-// (log2 units): P stays <= 2^8 in fp16 and O is rescaled rarely.
 constexpr float kRescaleSlack = 8.0f;
+constexpr int kGroupSlices = 8;  // heads sharing K/V stay together for L2 reuse
 
 template <int D>
 struct TcCfg {
-  static constexpr int kBoxes = D / 64;                 // 64-column swizzle boxes per tile row
-  static constexpr int kTileBytes = BN * D * 2;         // one K or V stage (== BM * D * 2)
-  static constexpr int kStages = (D == 128) ? 2 : 4;
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kQBytes = BM * D * 2;
+  static constexpr int kTileBytes = BN * D * 2;
+  static constexpr int kStages = (D == 128) ? 2 : 3;
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + BM * D * 2;
+  static constexpr int kKOff = kTiles * kQBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
-  static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 1 + 1;
+  static constexpr int kNumBars = 1 + 4 * kStages + 3 * kTiles + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
+  static constexpr uint32_t col_s(int t) { return 128u * t; }
+  static constexpr uint32_t col_o(int t) { return 256u + D * t; }
 };
 
 struct TcArgs {
   void* out;
   float* lse;
   const void* mask;
+  const uint8_t* mcls;  // boolean-mask tile classes [mslice][row_tile][col_block] or null
   int* status;
-  LeadTable mlt;  // mask offsets per slice
+  LeadTable mlt;        // mask element offsets per output slice
   int64_t L, S;
   int64_t m_rs, m_cs;
-  int32_t H, Hkv, group, m_blocks;
   int64_t slices;
+  int32_t H, Hkv, group, pairs;
+  int32_t row_tiles, col_blocks;
   int32_t causal;
-  float scale_log2;
+  float scale_log2, inv_scale;
 };
 
-template <typename MaskT>
-__device__ __forceinline__ float mask_add_value(const MaskT* p) {
-  return static_cast<float>(*p);
+// Index of the mask slice an output slice reads (only non-broadcast dims count).
+__host__ __device__ inline int64_t mask_slice_id(const LeadTable& t, int64_t slice) {
+  int64_t id = 0, rem = slice, suffix = 1;
+  for (int i = 0; i < t.n; ++i) suffix *= t.dim[i];
+  for (int i = 0; i < t.n; ++i) {
+    suffix /= t.dim[i];
+    const int64_t idx = rem / suffix;
+    rem %= suffix;
+    if (t.ms[i] != 0) id = id * t.dim[i] + idx;
+  }
+  return id;
 }
+
+__host__ __device__ inline int64_t mask_slice_count(const LeadTable& t) {
+  int64_t n = 1;
+  for (int i = 0; i < t.n; ++i)
+    if (t.ms[i] != 0) n *= t.dim[i];
+  return n;
+}
+
+template <typename MaskT>
+__device__ __forceinline__ float mask_value(const MaskT* p) { return static_cast<float>(*p); }
 template <>
-__device__ __forceinline__ float mask_add_value<__half>(const __half* p) { return __half2float(*p); }
+__device__ __forceinline__ float mask_value<__half>(const __half* p) { return __half2float(*p); }
 template <>
-__device__ __forceinline__ float mask_add_value<__nv_bfloat16>(const __nv_bfloat16* p) {
+__device__ __forceinline__ float mask_value<__nv_bfloat16>(const __nv_bfloat16* p) {
   return __bfloat162float(*p);
+}
+
+// Classify each (mask slice, 128-row tile, 128-key tile) of a boolean mask:
+// 0 = no element kept, 1 = every in-range element kept, 2 = mixed.
+__global__ void mask_classify_kernel(const uint8_t* mask, LeadTable mlt, int64_t L, int64_t S,
+                                     int64_t m_rs, int64_t m_cs, int32_t row_tiles,
+                                     int32_t col_blocks, uint8_t* cls) {
+  const int64_t tile = blockIdx.x;
+  const int cb = static_cast<int>(tile % col_blocks);
+  const int rt = static_cast<int>((tile / col_blocks) % row_tiles);
+  const int64_t ms = tile / (static_cast<int64_t>(col_blocks) * row_tiles);
+  // element offset of mask slice `ms`
+  int64_t off = 0, rem = ms;
+  for (int i = mlt.n - 1; i >= 0; --i) {
+    if (mlt.ms[i] == 0) continue;
+    off += (rem % mlt.dim[i]) * mlt.ms[i];
+    rem /= mlt.dim[i];
+  }
+  int any = 0, all = 1;
+  const int64_t r0 = static_cast<int64_t>(rt) * BM, c0 = static_cast<int64_t>(cb) * BN;
+  for (int e = threadIdx.x; e < BM * BN; e += blockDim.x) {
+    const int64_t r = r0 + e / BN, c = c0 + e % BN;
+    if (r < L && c < S) {
+      const int keep = mask[off + r * m_rs + c * m_cs] != 0;
+      any |= keep;
+      all &= keep;
+    }
+  }
+  any = __syncthreads_or(any);
+  all = __syncthreads_and(all);
+  if (threadIdx.x == 0) cls[tile] = any ? (all ? 1 : 2) : 0;
 }
 
 template <int D, bool BF16, int MASK, typename MaskT>
@@ -96,29 +161,67 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = k_full + C::kStages;
   uint64_t* v_full = k_empty + C::kStages;
   uint64_t* v_empty = v_full + C::kStages;
-  uint64_t* s_full = v_empty + C::kStages;  // [2]
-  uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* o_done = p_full + 2;
-  uint64_t* mma_done = o_done + 1;
+  uint64_t* s_full = v_empty + C::kStages;  // [kTiles]
+  uint64_t* p_full = s_full + kTiles;       // [kTiles]
+  uint64_t* o_done = p_full + kTiles;       // [kTiles]
+  uint64_t* mma_done = o_done + kTiles;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item: heaviest (last) query tiles first for causal balance.
-  const int64_t item = blockIdx.x;
-  const int m_block = a.m_blocks - 1 - static_cast<int>(item / a.slices);
-  const int64_t slice = item % a.slices;
-  const int64_t m0 = static_cast<int64_t>(m_block) * BM;
+  // Work item: groups of kGroupSlices heads (which share K/V under GQA) run
+  // together, heaviest query-tile pairs of the group first.
+  int64_t slice;
+  int pair;
+  {
+    const int64_t item = blockIdx.x;
+    const int64_t per_group = static_cast<int64_t>(kGroupSlices) * a.pairs;
+    const int64_t g = item / per_group;
+    const int64_t g0 = g * kGroupSlices;
+    const int64_t gsz = (a.slices - g0 < kGroupSlices) ? a.slices - g0 : kGroupSlices;
+    const int64_t rem = item - g * per_group;
+    pair = a.pairs - 1 - static_cast<int>(rem / gsz);
+    slice = g0 + rem % gsz;
+  }
+  const int64_t m0 = static_cast<int64_t>(pair) * (kTiles * BM);
   const int32_t zq = static_cast<int32_t>(slice);
   const int32_t zkv = static_cast<int32_t>((slice / a.H) * a.Hkv + (slice % a.H) / a.group);
+  const int64_t last_row = (m0 + kTiles * BM < a.L ? m0 + kTiles * BM : a.L) - 1;
   int64_t kv_end = a.S;
-  if (a.causal) {
-    const int64_t last_row = (m0 + BM < a.L ? m0 + BM : a.L) - 1;
-    kv_end = last_row + 1 < a.S ? last_row + 1 : a.S;
-  }
+  if (a.causal) kv_end = last_row + 1 < a.S ? last_row + 1 : a.S;
   const int n_blocks = static_cast<int>((kv_end + BN - 1) / BN);
+  const uint8_t* cls_row[kTiles] = {nullptr, nullptr};
+  if (MASK == PA_MASK_BOOL && a.mcls) {
+    const int64_t ms = mask_slice_id(a.mlt, slice);
+#pragma unroll
+    for (int t = 0; t < kTiles; ++t) {
+      const int64_t rt = (m0 / BM) + t;
+      cls_row[t] = rt < a.row_tiles ? a.mcls + (ms * a.row_tiles + rt) * a.col_blocks : nullptr;
+    }
+  }
+  // 0 dead, 1 full, 2 partial -- identical in every role.
+  auto tile_class = [&](int t, int j) -> int {
+    const int64_t r_lo = m0 + static_cast<int64_t>(t) * BM;
+    if (r_lo >= a.L) return 0;
+    const int64_t r_hi = (r_lo + BM - 1 < a.L) ? r_lo + BM - 1 : a.L - 1;
+    const int64_t n0 = static_cast<int64_t>(j) * BN;
+    int c = 1;
+    if (a.causal) {
+      if (n0 > r_hi) return 0;
+      if (n0 + BN - 1 > r_lo) c = 2;
+    }
+    if (n0 + BN > a.S) c = 2;
+    if (MASK == PA_MASK_ADD) c = 2;
+    if (MASK == PA_MASK_BOOL) {
+      const int mc = cls_row[t] ? cls_row[t][j] : 2;
+      if (mc == 0) return 0;
+      if (mc == 2) c = 2;
+    }
+    return c;
+  };
+  auto block_live = [&](int j) -> bool { return tile_class(0, j) != 0 || tile_class(1, j) != 0; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -128,16 +231,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(v_full + s, 1);
       mbar_init(v_empty + s, 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(s_full + s, 1);
-      mbar_init(p_full + s, 128);
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(s_full + t, 1);
+      mbar_init(p_full + t, 128);
+      mbar_init(o_done + t, 1);
     }
-    mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -146,34 +249,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_blocks > 0) {
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_expect_tx(q_full, BM * D * 2);
-      for (int b = 0; b < C::kBoxes; ++b)
-        tma_load_3d(sQ + b * (BM * 128), &tq, q_full, b * 64, static_cast<int32_t>(m0), zq);
+      mbar_expect_tx(q_full, kTiles * C::kQBytes);
+      for (int t = 0; t < kTiles; ++t)
+        for (int b = 0; b < C::kBoxes; ++b)
+          tma_load_3d(sQ + t * C::kQBytes + b * (BM * 128), &tq, q_full, b * 64,
+                      static_cast<int32_t>(m0 + t * BM), zq);
       int last_k[C::kStages], last_v[C::kStages];
 #pragma unroll
       for (int s = 0; s < C::kStages; ++s) last_k[s] = last_v[s] = -1;
+      int i = 0;
       for (int j = 0; j < n_blocks; ++j) {
-        const int st = j % C::kStages;
-        const uint32_t ph = (j / C::kStages) & 1;
+        if (!block_live(j)) continue;
+        const int st = i % C::kStages;
+        const uint32_t ph = (i / C::kStages) & 1;
         if (!mbar_wait(k_empty + st, ph ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
         mbar_expect_tx(k_full + st, C::kTileBytes);
         for (int b = 0; b < C::kBoxes; ++b)
           tma_load_3d(sK + st * C::kTileBytes + b * (BN * 128), &tk, k_full + st, b * 64, j * BN, zkv);
-        last_k[st] = j;
+        last_k[st] = i;
         if (!mbar_wait(v_empty + st, ph ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
         mbar_expect_tx(v_full + st, C::kTileBytes);
         for (int b = 0; b < C::kBoxes; ++b)
           tma_load_3d(sV + st * C::kTileBytes + b * (BN * 128), &tv, v_full + st, b * 64, j * BN, zkv);
-        last_v[st] = j;
+        last_v[st] = i;
+        ++i;
       }
-      // Every issued copy must land before the CTA may exit. A full barrier
-      // completes once per issue, so wait for the last issue of each stage.
       mbar_drain(q_full, 0);
 #pragma unroll
       for (int s = 0; s < C::kStages; ++s) {
@@ -182,79 +288,105 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA issue
     if (lane == 0 && n_blocks > 0) {
       constexpr uint32_t idS = idesc_f16(BM, BN, false, false, BF16);
       constexpr uint32_t idO = idesc_f16(BM, D, false, true, BF16);
       const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, a.status, kStatusTimeoutLoad, abort_flag);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % C::kStages;
-        const uint32_t ph = (i / C::kStages) & 1;
-        const uint32_t sb = i & 1;
-        if (!mbar_wait(p_full + sb, (i >> 1) & 1, a.status, kStatusTimeoutSoftmax, abort_flag)) return false;
-        if (!mbar_wait(v_full + st, ph, a.status, kStatusTimeoutLoad, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + st * C::kTileBytes);
-        const uint32_t p_col = tmem + (sb ? kColS1 : kColS0);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bdesc = sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024);
-          umma_ts(tmem + kColO, p_col + kk * 8, bdesc, idO, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(o_done);
-        tc_commit(v_empty + st);
-        return true;
-      };
-      for (int j = 0; ok && j < n_blocks; ++j) {
-        const int st = j % C::kStages;
-        const uint32_t ph = (j / C::kStages) & 1;
-        const uint32_t sb = j & 1;
-        if (!mbar_wait(k_full + st, ph, a.status, kStatusTimeoutLoad, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      int cnt[kTiles] = {0, 0};   // S issued per tile
+      int pv_cnt[kTiles] = {0, 0};
+      int pend1 = -1;             // union index of tile 1's S awaiting its PV
+      bool pend1_solo = false;    // tile 0 was dead in that block (V release owed by tile 1)
+      auto issue_s = [&](int t, int st) {
         const uint32_t k_addr = smem_u32(sK + st * C::kTileBytes);
+        const uint32_t qa = q_addr + t * C::kQBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t box = kk / 4, sub = (kk % 4) * 32;
-          const uint64_t adesc = sdesc_sw128(q_addr + box * (BM * 128) + sub, 16, 1024);
-          const uint64_t bdesc = sdesc_sw128(k_addr + box * (BN * 128) + sub, 16, 1024);
-          umma_ss(tmem + (sb ? kColS1 : kColS0), adesc, bdesc, idS, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + C::col_s(t), sdesc_sw128(qa + box * (BM * 128) + sub, 16, 1024),
+                  sdesc_sw128(k_addr + box * (BN * 128) + sub, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
-        tc_commit(s_full + sb);
-        tc_commit(k_empty + st);
-        if (j >= 1 && !issue_pv(j - 1)) {
+        tc_commit(s_full + t);
+        ++cnt[t];
+      };
+      auto issue_pv = [&](int t, int i, bool release_v) -> bool {
+        const int st = i % C::kStages;
+        if (!mbar_wait(p_full + t, pv_cnt[t] & 1, a.status, kStatusTimeoutSoftmax, abort_flag)) return false;
+        if (!mbar_wait(v_full + st, (i / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + st * C::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8,
+                  sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024), idO,
+                  (pv_cnt[t] > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(o_done + t);
+        if (release_v) tc_commit(v_empty + st);
+        ++pv_cnt[t];
+        return true;
+      };
+      int i = 0;
+      for (int j = 0; ok && j < n_blocks; ++j) {
+        if (!block_live(j)) continue;
+        const int st = i % C::kStages;
+        const bool live0 = tile_class(0, j) != 0, live1 = tile_class(1, j) != 0;
+        if (!mbar_wait(k_full + st, (i / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) {
           ok = false;
           break;
         }
+        tc_fence_after();
+        if (live0) issue_s(0, st);
+        if (pend1 >= 0) {
+          // tile 1's previous block; its V stage is released here
+          if (!issue_pv(1, pend1, true)) {
+            ok = false;
+            break;
+          }
+          pend1 = -1;
+        }
+        if (live1) {
+          issue_s(1, st);
+          pend1 = i;
+          pend1_solo = !live0;
+        }
+        tc_commit(k_empty + st);
+        if (live0 && !issue_pv(0, i, !live1)) {
+          ok = false;
+          break;
+        }
+        ++i;
       }
-      if (ok) issue_pv(n_blocks - 1);
-      // All issued tensor-core work must finish before TMEM is freed.
+      (void)pend1_solo;
+      if (ok && pend1 >= 0) issue_pv(1, pend1, true);
       tc_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
     __syncwarp();
   } else {
     // --------------------------------------------------------------- softmax
+    const int t = warp / 4;                 // query tile of this warpgroup
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // row inside the tile == TMEM lane
-    const int64_t row = m0 + r;
+    const int r = quad * 32 + lane;         // row inside the tile == TMEM lane
+    const int64_t row = m0 + static_cast<int64_t>(t) * BM + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t s_addr = lane_base + C::col_s(t);
+    const uint32_t o_addr = lane_base + C::col_o(t);
     const bool row_ok = row < a.L;
+    const float sl2 = a.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
     const SliceOffsets moff = slice_offsets(a.mlt, slice);
+    int cnt = 0;
     bool ok = true;
 
     for (int j = 0; j < n_blocks; ++j) {
-      const uint32_t sb = j & 1;
-      ok = mbar_wait(s_full + sb, (j >> 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
+      const int cls = tile_class(t, j);
+      if (cls == 0) continue;
+      ok = mbar_wait(s_full + t, cnt & 1, a.status, kStatusTimeoutMma, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t s_addr = lane_base + (sb ? kColS1 : kColS0);
       float x[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
@@ -262,88 +394,96 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(s_addr + c * 32, rr);
         tmem_ld_wait();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) x[c * 32 + t] = __uint_as_float(rr[t]) * a.scale_log2;
+        for (int u = 0; u < 32; ++u) x[c * 32 + u] = __uint_as_float(rr[u]);
       }
       const int64_t n0 = static_cast<int64_t>(j) * BN;
-      const bool edge = (n0 + BN > a.S) || (a.causal && n0 + BN - 1 > m0);
-      if (edge || MASK != PA_MASK_NONE) {
+      if (cls == 2) {
         const int64_t vis = a.causal ? (row + 1 < a.S ? row + 1 : a.S) : a.S;
+        const int lim = static_cast<int>(vis - n0 < 0 ? 0 : (vis - n0 > BN ? BN : vis - n0));
 #pragma unroll
-        for (int t = 0; t < BN; ++t) {
-          const int64_t col = n0 + t;
-          if (col >= vis) x[t] = -INFINITY;
-        }
+        for (int u = 0; u < BN; ++u)
+          if (u >= lim) x[u] = -INFINITY;
         if (MASK != PA_MASK_NONE && row_ok) {
-          const int64_t base = moff.m + row * a.m_rs;
+          const int64_t base = moff.m + row * a.m_rs + n0 * a.m_cs;
+          if (MASK == PA_MASK_BOOL) {
+            const uint8_t* mp = static_cast<const uint8_t*>(a.mask) + base;
+            if (a.m_cs == 1 && n0 + BN <= a.S && (reinterpret_cast<uintptr_t>(mp) & 15) == 0) {
 #pragma unroll
-          for (int t = 0; t < BN; ++t) {
-            const int64_t col = n0 + t;
-            if (col < a.S) {
-              if (MASK == PA_MASK_BOOL) {
-                if (!static_cast<const uint8_t*>(a.mask)[base + col * a.m_cs]) x[t] = -INFINITY;
-              } else {
-                x[t] += kLog2e * mask_add_value(static_cast<const MaskT*>(a.mask) + base + col * a.m_cs);
+              for (int v = 0; v < BN / 16; ++v) {
+                const uint4 w = reinterpret_cast<const uint4*>(mp)[v];
+                const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int b = 0; b < 16; ++b)
+                  if (((wd[b >> 2] >> (8 * (b & 3))) & 0xffu) == 0u) x[v * 16 + b] = -INFINITY;
               }
+            } else {
+#pragma unroll
+              for (int u = 0; u < BN; ++u)
+                if (u < lim && mp[u * a.m_cs] == 0) x[u] = -INFINITY;
             }
+          } else {
+            const MaskT* mp = static_cast<const MaskT*>(a.mask) + base;
+#pragma unroll
+            for (int u = 0; u < BN; ++u)
+              if (u < lim) x[u] = fmaf(mask_value(mp + u * a.m_cs), a.inv_scale, x[u]);
           }
         }
       }
-      float mx = x[0];
+      // Row max of raw scores (scale > 0), eight partial chains.
+      float mx8[8];
 #pragma unroll
-      for (int t = 1; t < BN; ++t) mx = fmaxf(mx, x[t]);
+      for (int u = 0; u < 8; ++u) mx8[u] = x[u];
+#pragma unroll
+      for (int u = 8; u < BN; ++u) mx8[u & 7] = fmaxf(mx8[u & 7], x[u]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
       const float m_new = fmaxf(m_run, mx);
       const float m_use = (m_run == -INFINITY || m_new - m_run > kRescaleSlack) ? m_new : m_run;
-      float rowsum = 0.f;
-      uint32_t pk[BN / 2];
-      if (m_use == -INFINITY) {
+      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+      float sum8[8];
 #pragma unroll
-        for (int t = 0; t < BN / 2; ++t) pk[t] = 0u;
-      } else {
+      for (int u = 0; u < 8; ++u) sum8[u] = 0.f;
 #pragma unroll
-        for (int t = 0; t < BN / 2; ++t) {
-          const float p0 = ex2(x[2 * t] - m_use);
-          const float p1 = ex2(x[2 * t + 1] - m_use);
-          rowsum += p0 + p1;
-          pk[t] = pack2(p0, p1, BF16);
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float p0 = ex2(fmaf(x[c * 32 + 2 * u], sl2, neg_m));
+          const float p1 = ex2(fmaf(x[c * 32 + 2 * u + 1], sl2, neg_m));
+          sum8[u & 7] += p0 + p1;
+          pk[u] = pack2(p0, p1, BF16);
         }
+        tmem_st16(s_addr + c * 16, pk);
       }
-      {
-        uint32_t half0[32], half1[32];
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          half0[t] = pk[t];
-          half1[t] = pk[32 + t];
-        }
-        tmem_st32(s_addr, half0);
-        tmem_st32(s_addr + 32, half1);
-        tmem_st_wait();
-      }
+      tmem_st_wait();
+      const float rowsum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       const float alpha = (m_use == m_run) ? 1.f : ((m_run == -INFINITY) ? 0.f : ex2(m_run - m_use));
-      const bool need = (j > 0) && (m_use != m_run);
+      const bool need = (cnt > 0) && (m_use != m_run);
       if (__any_sync(0xffffffffu, need)) {
-        ok = mbar_wait(o_done, (j - 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
+        ok = mbar_wait(o_done + t, (cnt - 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t rr[32];
-          tmem_ld32(lane_base + kColO + c * 32, rr);
+          tmem_ld32(o_addr + c * 32, rr);
           tmem_ld_wait();
 #pragma unroll
-          for (int t = 0; t < 32; ++t) rr[t] = __float_as_uint(__uint_as_float(rr[t]) * alpha);
-          tmem_st32(lane_base + kColO + c * 32, rr);
+          for (int u = 0; u < 32; ++u) rr[u] = __float_as_uint(__uint_as_float(rr[u]) * alpha);
+          tmem_st32(o_addr + c * 32, rr);
         }
         tmem_st_wait();
       }
       l_run = l_run * alpha + rowsum;
       m_run = m_use;
       tc_fence_before();
-      mbar_arrive(p_full + sb);
+      mbar_arrive(p_full + t);
+      ++cnt;
     }
 
-    if (ok && n_blocks > 0) {
-      ok = mbar_wait(o_done, (n_blocks - 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
+    if (ok && cnt > 0) {
+      ok = mbar_wait(o_done + t, (cnt - 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
@@ -353,21 +493,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t rr[32];
-        if (n_blocks > 0) {
-          tmem_ld32(lane_base + kColO + c * 32, rr);
+        if (cnt > 0) {
+          tmem_ld32(o_addr + c * 32, rr);
           tmem_ld_wait();
         } else {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) rr[t] = 0u;
+          for (int u = 0; u < 32; ++u) rr[u] = 0u;
         }
         uint32_t pk[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t)
-          pk[t] = pack2(__uint_as_float(rr[2 * t]) * inv, __uint_as_float(rr[2 * t + 1]) * inv, BF16);
+        for (int u = 0; u < 16; ++u)
+          pk[u] = pack2(__uint_as_float(rr[2 * u]) * inv, __uint_as_float(rr[2 * u + 1]) * inv, BF16);
         if (row_ok) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
 #pragma unroll
-          for (int t = 0; t < 4; ++t) dst[t] = make_uint4(pk[4 * t], pk[4 * t + 1], pk[4 * t + 2], pk[4 * t + 3]);
+          for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
       }
       if (row_ok && a.lse)
@@ -377,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -445,6 +585,7 @@ bool fwd_tc_eligible(const pa_sdpa_desc& d, std::string* why) {
   };
   if (d.dtype != PA_F16 && d.dtype != PA_BF16) return no("dtype is not fp16/bf16");
   if (d.E != d.Ev || (d.E != 64 && d.E != 128)) return no("head dim not 64/128 or E != Ev");
+  if (!(d.scale > 0)) return no("scale must be positive");
   int64_t n, H, Hkv;
   if (!dense_bhsd(d, &n, &H, &Hkv)) return no("operands are not dense (B, H, L, D)");
   if (n > 0x7fffffffLL / 64 || d.L > 0x7fffffffLL || d.S > 0x7fffffffLL) return no("too large");
@@ -478,21 +619,40 @@ pa_status launch_fwd_tc(const pa_sdpa_desc& d, const void* q, const void* k, con
   a.S = d.S;
   a.m_rs = d.m_row_stride;
   a.m_cs = d.m_col_stride;
+  a.slices = n;
   a.H = static_cast<int32_t>(H);
   a.Hkv = static_cast<int32_t>(Hkv);
   a.group = static_cast<int32_t>(H / Hkv);
-  a.m_blocks = static_cast<int32_t>((d.L + BM - 1) / BM);
-  a.slices = n;
+  a.pairs = static_cast<int32_t>((d.L + kTiles * BM - 1) / (kTiles * BM));
+  a.row_tiles = static_cast<int32_t>((d.L + BM - 1) / BM);
+  a.col_blocks = static_cast<int32_t>((d.S + BN - 1) / BN);
   a.causal = d.is_causal;
   a.scale_log2 = static_cast<float>(d.scale * 1.4426950408889634);
-  const int64_t grid = n * a.m_blocks;
+  a.inv_scale = static_cast<float>(1.0 / d.scale);
+  const int64_t grid = n * a.pairs;
   if (grid == 0) return PA_OK;
   if (grid > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "fwd_tc: grid too large");
+  uint8_t* cls = nullptr;
+  if (!d.is_causal && d.mask_kind == PA_MASK_BOOL) {
+    const int64_t tiles = mask_slice_count(a.mlt) * a.row_tiles * a.col_blocks;
+    if (tiles > 0 && tiles <= 0x7fffffffLL) {
+      PA_TRY(scratch_alloc(reinterpret_cast<void**>(&cls), static_cast<size_t>(tiles), st));
+      mask_classify_kernel<<<static_cast<unsigned>(tiles), 256, 0, st>>>(
+          static_cast<const uint8_t*>(mask), a.mlt, d.L, d.S, d.m_row_stride, d.m_col_stride,
+          a.row_tiles, a.col_blocks, cls);
+      PA_CUDA(cudaGetLastError());
+      a.mcls = cls;
+    }
+  }
+  pa_status rc;
   if (D == 128)
-    return bf16 ? launch_masked<128, true>(d, tq, tk, tv, a, grid, st)
-                : launch_masked<128, false>(d, tq, tk, tv, a, grid, st);
-  return bf16 ? launch_masked<64, true>(d, tq, tk, tv, a, grid, st)
+    rc = bf16 ? launch_masked<128, true>(d, tq, tk, tv, a, grid, st)
+              : launch_masked<128, false>(d, tq, tk, tv, a, grid, st);
+  else
+    rc = bf16 ? launch_masked<64, true>(d, tq, tk, tv, a, grid, st)
               : launch_masked<64, false>(d, tq, tk, tv, a, grid, st);
+  scratch_free(cls, st);
+  return rc;
 }
 
 }  // namespace pa
