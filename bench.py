@@ -201,8 +201,8 @@ def cpu_sample(name, budget_s=12.0, x=None):
             x = workloads.make(name)
         jobs = []
         rng = np.random.default_rng(0)
-        for r0 in sorted(rng.integers(0, w.q_shape[2] // 64, size=4 * threads) * 64):
-            h = int(rng.integers(0, w.q_shape[1]))
+        for r0 in sorted(rng.integers(0, x["q"].shape[2] // 64, size=4 * threads) * 64):
+            h = int(rng.integers(0, x["q"].shape[1]))
             rows = np.arange(r0, r0 + 64)
             keys = r0 + 64
             m = np.arange(keys)[None, :] <= rows[:, None]
@@ -267,19 +267,49 @@ def run_reference(args):
     return 0
 
 
-def workload_config(name, n):
+def workload_config(name, n, x=None):
     from pa_b200 import workloads
 
     w = workloads.WORKLOADS[name]
-    return {"workload": f"{name}: q {w.q_shape} k/v {w.kv_shape} {w.dtype}"
+    qs = tuple(x["q"].shape) if x is not None else w.q_shape
+    ks = tuple(x["k"].shape) if x is not None else w.kv_shape
+    return {"workload": f"{name}: q {qs} k/v {ks} {w.dtype}"
                         f"{' causal' if w.is_causal else ''}{' gqa' if w.enable_gqa else ''}"
                         f"{' key-padding mask' if w.masked else ''}",
-            "global_batch": w.q_shape[0] * n, "seq_len": w.q_shape[2],
+            "global_batch": qs[0] * n, "seq_len": qs[2],
             "parallelism": f"batch-shard x{n}" if n > 1 else "single",
             "l2": "inputs larger than L2 (no flush)"}
 
 
 # ---------------------------------------------------------------- GPU leg
+
+def shrink(x, w, batch=None, heads=None):
+    """Keep the first ``batch`` rows / ``heads`` query heads (and their KV heads) of a workload."""
+    if not batch and not heads:
+        return x
+    group = w.q_shape[1] // w.kv_shape[1]
+    b = slice(0, batch) if batch else slice(None)
+    hq = slice(0, heads) if heads else slice(None)
+    hk = slice(0, max(1, heads // group)) if heads else slice(None)
+    out = {}
+    for key, val in x.items():
+        if key in ("q", "dout"):
+            out[key] = np.ascontiguousarray(val[b, hq])
+        elif key in ("k", "v"):
+            out[key] = np.ascontiguousarray(val[b, hk])
+        elif key == "mask":
+            out[key] = np.ascontiguousarray(val[b])
+        elif key == "keep":
+            out[key] = val[b]
+    return out
+
+
+def fwd_flops(x, w):
+    """Algorithmic forward FLOPs of the (possibly shrunk) inputs: 4 B Hq Lq Lk D, halved if causal."""
+    bq, hq, lq, d = x["q"].shape
+    f = 4.0 * bq * hq * lq * x["k"].shape[2] * d
+    return f / 2 if w.is_causal else f
+
 
 def run_gpu(args):
     rank, local, world, pg = dist_setup(args.gpus)
@@ -295,12 +325,12 @@ def run_gpu(args):
     w = workloads.WORKLOADS[args.workload]
     if w.backward and world > 1:
         return run_ring(args, rank, local, world, pg)
-    x = workloads.make(args.workload)
+    x = shrink(workloads.make(args.workload), w, args.batch, args.heads)
     mask = x.get("mask")
     plan = pa_b200.plan_call(x["q"].shape, x["k"].shape, x["v"].shape, x["q"].dtype, x["k"].dtype,
                              x["v"].dtype, None if mask is None else mask.shape,
                              None if mask is None else mask.dtype, w.is_causal, None,
-                             w.q_shape[1] // w.kv_shape[1])
+                             x["q"].shape[1] // x["k"].shape[1])
     decode = use_decode_kernel(plan)
     backward = w.backward
     stream = Stream()
@@ -378,23 +408,23 @@ def run_gpu(args):
         launches = 2
     elif backward:
         unit = "TFLOP/s"
-        work = w.flops_fwd + w.flops_bwd
+        work = 3.5 * fwd_flops(x, w)
         value = world * work / (ms * 1e-3) / 1e12
         fwd_ms = statistics.mean(events[i].elapsed_ms(mids[i]) for i in range(args.steps))
         bwd_ms = statistics.mean(mids[i].elapsed_ms(events[i + 1]) for i in range(args.steps))
         peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
-        achieved = w.flops_bwd / (bwd_ms * 1e-3) / 1e12
+        achieved = 2.5 * fwd_flops(x, w) / (bwd_ms * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": traffic_for(args.workload),
                 "peak_kind": pk_kind + " (sustained: seconds-long step)",
                 "kernel": "backward: bwd_prep + bwd_dkdv + bwd_dq (2.5x forward FLOPs)"}
         extra = {"fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
-                 "fwd_tflops": w.flops_fwd / (fwd_ms * 1e-3) / 1e12,
+                 "fwd_tflops": fwd_flops(x, w) / (fwd_ms * 1e-3) / 1e12,
                  "bwd_tflops": achieved}
         launches = 4
     else:
         unit = "TFLOP/s"
-        work = w.flops_fwd
+        work = fwd_flops(x, w)
         value = world * work / (ms * 1e-3) / 1e12
         achieved = work / (statistics.mean(per) * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
@@ -440,7 +470,7 @@ def run_gpu(args):
         "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16" if plan.cdt == np.float16 else str(plan.cdt).replace("float", "f"),
-        "data": "synthetic", "config": workload_config(args.workload, world),
+        "data": "synthetic", "config": workload_config(args.workload, world, x),
         "roofline": roof,
         "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
@@ -588,6 +618,10 @@ def main():
     ap.add_argument("--workload", default="fp16_causal_gqa")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="keep only the first BATCH batch rows of the workload (profiling)")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="keep only the first HEADS query heads (and their KV heads)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
