@@ -295,32 +295,46 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       const float* l2 = reinterpret_cast<const float*>(stage_ptr(st) + 2 * C::kQBytes);
       const float* dl = l2 + BQ;
       const int64_t q0 = static_cast<int64_t>(qb0 + i % per_head) * BQ;
-      uint32_t pk[32], dk[32];
+      // Visible query columns of this key row: c in [cmin, cmax).
+      const int64_t lo = a.causal ? key - q0 : 0;
+      const int cmin = static_cast<int>(lo < 0 ? 0 : (lo > BQ ? BQ : lo));
+      const int64_t hi = a.L - q0;
+      const int cmax = static_cast<int>(hi < 0 ? 0 : (hi > BQ ? BQ : hi));
+      const bool all_vis = __all_sync(0xffffffffu, cmin == 0 && cmax == BQ);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t sr[32], pr[32];
         tmem_ld32(lane_base + C::kColS + sb * 64 + half * 32, sr);
         tmem_ld32(lane_base + C::kColP + sb * 64 + half * 32, pr);
         tmem_ld_wait();
+        reg_fence(sr);
+        reg_fence(pr);
+        uint32_t pk[16], dk[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          float p2[2], d2[2];
+        for (int v4 = 0; v4 < 8; ++v4) {
+          const float4 lz = reinterpret_cast<const float4*>(l2)[half * 8 + v4];
+          const float4 dd = reinterpret_cast<const float4*>(dl)[half * 8 + v4];
+          const float lzv[4] = {lz.x, lz.y, lz.z, lz.w};
+          const float ddv[4] = {dd.x, dd.y, dd.z, dd.w};
+          float p4[4], d4[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = half * 32 + 2 * t + u;
-            const int64_t qrow = q0 + c;
-            const float lz = l2[c];
-            const bool vis = qrow < a.L && (!a.causal || key <= qrow) && lz != -INFINITY;
-            const float p = vis ? ex2(__uint_as_float(sr[2 * t + u]) * a.scale_log2 - lz) : 0.f;
-            p2[u] = p;
-            d2[u] = vis ? p * (__uint_as_float(pr[2 * t + u]) - dl[c]) : 0.f;
+          for (int u = 0; u < 4; ++u) {
+            const int e = v4 * 4 + u;          // column inside this half
+            const int c = half * 32 + e;       // column inside the block
+            float p = ex2(fmaf(__uint_as_float(sr[e]), a.scale_log2, -lzv[u]));
+            if (!all_vis) p = (c >= cmin && c < cmax && lzv[u] != -INFINITY) ? p : 0.f;
+            p4[u] = p;
+            d4[u] = p * (__uint_as_float(pr[e]) - ddv[u]);
+            if (!all_vis && !(c >= cmin && c < cmax)) d4[u] = 0.f;
           }
-          pk[half * 16 + t] = pack2(p2[0], p2[1], BF16);
-          dk[half * 16 + t] = pack2(d2[0], d2[1], BF16);
+          pk[v4 * 2] = pack2(p4[0], p4[1], BF16);
+          pk[v4 * 2 + 1] = pack2(p4[2], p4[3], BF16);
+          dk[v4 * 2] = pack2(d4[0], d4[1], BF16);
+          dk[v4 * 2 + 1] = pack2(d4[2], d4[3], BF16);
         }
+        tmem_st16(lane_base + C::kColS + sb * 64 + half * 16, pk);
+        tmem_st16(lane_base + C::kColP + sb * 64 + half * 16, dk);
       }
-      tmem_st32(lane_base + C::kColS + sb * 64, pk);
-      tmem_st32(lane_base + C::kColP + sb * 64, dk);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(ds_ready + sb);
@@ -341,6 +355,8 @@ __global__ void __launch_bounds__(kThreadsB, 1)
           tmem_ld32(lane_base + C::kColV + c * 32, rv);
           tmem_ld32(lane_base + C::kColK + c * 32, rk);
           tmem_ld_wait();
+          reg_fence(rv);
+          reg_fence(rk);
         } else {
 #pragma unroll
           for (int t = 0; t < 32; ++t) rv[t] = rk[t] = 0u;
@@ -535,27 +551,33 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       tc_fence_after();
       const int64_t k0 = static_cast<int64_t>(j) * BK;
       const int64_t vis = a.causal ? (row + 1 < a.S ? row + 1 : a.S) : a.S;
-      uint32_t dk[32];
+      const int64_t lim64 = row_live ? vis - k0 : 0;
+      const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > BK ? BK : lim64));
+      const bool all_vis = __all_sync(0xffffffffu, lim == BK);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t sr[32], pr[32];
         tmem_ld32(lane_base + C::kColS + sb * 64 + half * 32, sr);
         tmem_ld32(lane_base + C::kColP + sb * 64 + half * 32, pr);
         tmem_ld_wait();
+        reg_fence(sr);
+        reg_fence(pr);
+        uint32_t dk[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
           float d2[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int c = half * 32 + 2 * t + u;
-            const bool vis_c = row_live && (k0 + c) < vis;
-            const float p = vis_c ? ex2(__uint_as_float(sr[2 * t + u]) * a.scale_log2 - lz) : 0.f;
-            d2[u] = vis_c ? p * (__uint_as_float(pr[2 * t + u]) - dlt) : 0.f;
+            const float p = ex2(fmaf(__uint_as_float(sr[2 * t + u]), a.scale_log2, -lz));
+            float d = p * (__uint_as_float(pr[2 * t + u]) - dlt);
+            if (!all_vis && c >= lim) d = 0.f;
+            d2[u] = d;
           }
-          dk[half * 16 + t] = pack2(d2[0], d2[1], BF16);
+          dk[t] = pack2(d2[0], d2[1], BF16);
         }
+        tmem_st16(lane_base + C::kColP + sb * 64 + half * 16, dk);
       }
-      tmem_st32(lane_base + C::kColP + sb * 64, dk);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(ds_ready + sb);
@@ -573,6 +595,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         if (n > 0) {
           tmem_ld32(lane_base + C::kColQ + c * 32, rq);
           tmem_ld_wait();
+          reg_fence(rq);
         } else {
 #pragma unroll
           for (int t = 0; t < 32; ++t) rq[t] = 0u;
@@ -649,10 +672,8 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
       a.blocks = static_cast<int32_t>((S + C::BK - 1) / C::BK);
       const int64_t grid = nkv * a.blocks;
       auto kern = bwd_dkdv_kernel<D, BF16>;
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess) {
-        rc = fail(PA_ERR_CUDA, "bwd_dkdv: shared memory attribute");
-        break;
-      }
+      static uint64_t attr_set = 0;
+      if ((rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), C::kSmemBytes, &attr_set)) != PA_OK) break;
       if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tq64, tdo64, tk128, tv128, a);
       if (cudaGetLastError() != cudaSuccess) {
         rc = fail(PA_ERR_CUDA, "bwd_dkdv launch failed");
@@ -665,10 +686,8 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
       a.blocks = static_cast<int32_t>((L + C::BQ - 1) / C::BQ);
       const int64_t grid = n * a.blocks;
       auto kern = bwd_dq_kernel<D, BF16>;
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess) {
-        rc = fail(PA_ERR_CUDA, "bwd_dq: shared memory attribute");
-        break;
-      }
+      static uint64_t attr_set = 0;
+      if ((rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), C::kSmemBytes, &attr_set)) != PA_OK) break;
       if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tq128, tdo128, tk64, tv64, a);
       if (cudaGetLastError() != cudaSuccess) {
         rc = fail(PA_ERR_CUDA, "bwd_dq launch failed");

@@ -71,7 +71,32 @@ int sm_count() {
 pa_status scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
   *p = nullptr;
   if (bytes == 0) return PA_OK;
+  {
+    // Keep freed scratch cached in the device's default pool instead of
+    // returning it to the driver at every synchronisation.
+    static uint64_t pool_set = 0;
+    const int d = current_device();
+    if (d >= 0 && d < 64 && !(pool_set & (1ull << d))) {
+      std::lock_guard<std::mutex> lk(g_mu);
+      cudaMemPool_t pool;
+      if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) {
+        uint64_t keep = ~0ull;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      }
+      cudaGetLastError();
+      pool_set |= 1ull << d;
+    }
+  }
   PA_CUDA(cudaMallocAsync(p, bytes, s));
+  return PA_OK;
+}
+
+pa_status set_smem_attr_once(const void* fn, int bytes, uint64_t* mask) {
+  const int d = current_device();
+  const uint64_t bit = (d >= 0 && d < 64) ? (1ull << d) : 0;
+  if (bit && (__atomic_load_n(mask, __ATOMIC_ACQUIRE) & bit)) return PA_OK;
+  PA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (bit) __atomic_fetch_or(mask, bit, __ATOMIC_RELEASE);
   return PA_OK;
 }
 

@@ -377,7 +377,8 @@ pa_status launch_dec(const DecPlan& p, const CUtensorMap& tk, const CUtensorMap&
                      void* out, float* lse, cudaStream_t st) {
   auto kern = decode_partial_kernel<D, G, BF16>;
   constexpr int smem = DecCfg<D>::kSmemBytes;
-  PA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  static uint64_t attr_set = 0;
+  PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, &attr_set));
   const int64_t grid = p.B * p.Hkv * p.nsplit;
   kern<<<static_cast<unsigned>(grid), kThreadsDec, smem, st>>>(tk, tv, a);
   PA_CUDA(cudaGetLastError());

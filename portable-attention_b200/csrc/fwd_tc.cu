@@ -130,12 +130,29 @@ __global__ void mask_classify_kernel(const uint8_t* mask, LeadTable mlt, int64_t
   }
   int any = 0, all = 1;
   const int64_t r0 = static_cast<int64_t>(rt) * BM, c0 = static_cast<int64_t>(cb) * BN;
-  for (int e = threadIdx.x; e < BM * BN; e += blockDim.x) {
-    const int64_t r = r0 + e / BN, c = c0 + e % BN;
-    if (r < L && c < S) {
-      const int keep = mask[off + r * m_rs + c * m_cs] != 0;
-      any |= keep;
-      all &= keep;
+  const bool vec = m_cs == 1 && c0 + BN <= S && ((off + c0) & 15) == 0 && (m_rs & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(mask) & 15) == 0;
+  if (vec) {
+    // 16 bytes per load; a word has a zero byte iff (w - 0x01..) & ~w & 0x80.. != 0.
+    for (int e = threadIdx.x; e < BM * (BN / 16); e += blockDim.x) {
+      const int64_t r = r0 + e / (BN / 16);
+      if (r >= L) continue;
+      const uint4 w = *reinterpret_cast<const uint4*>(mask + off + r * m_rs + c0 + (e % (BN / 16)) * 16);
+      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        any |= wd[k] != 0u;
+        all &= ((wd[k] - 0x01010101u) & ~wd[k] & 0x80808080u) == 0u;
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < BM * BN; e += blockDim.x) {
+      const int64_t r = r0 + e / BN, c = c0 + e % BN;
+      if (r < L && c < S) {
+        const int keep = mask[off + r * m_rs + c * m_cs] != 0;
+        any |= keep;
+        all &= keep;
+      }
     }
   }
   any = __syncthreads_or(any);
@@ -388,13 +405,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       float x[BN];
+      {
+        uint32_t rr[BN / 32][32];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(s_addr + c * 32, rr);
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_addr + c * 32, rr[c]);
         tmem_ld_wait();
 #pragma unroll
-        for (int u = 0; u < 32; ++u) x[c * 32 + u] = __uint_as_float(rr[u]);
+        for (int c = 0; c < BN / 32; ++c) {
+          reg_fence(rr[c]);
+#pragma unroll
+          for (int u = 0; u < 32; ++u) x[c * 32 + u] = __uint_as_float(rr[c][u]);
+        }
       }
       const int64_t n0 = static_cast<int64_t>(j) * BN;
       if (cls == 2) {
@@ -469,6 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t rr[32];
           tmem_ld32(o_addr + c * 32, rr);
           tmem_ld_wait();
+          reg_fence(rr);
 #pragma unroll
           for (int u = 0; u < 32; ++u) rr[u] = __float_as_uint(__uint_as_float(rr[u]) * alpha);
           tmem_st32(o_addr + c * 32, rr);
@@ -496,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cnt > 0) {
           tmem_ld32(o_addr + c * 32, rr);
           tmem_ld_wait();
+          reg_fence(rr);
         } else {
 #pragma unroll
           for (int u = 0; u < 32; ++u) rr[u] = 0u;
@@ -528,7 +551,8 @@ pa_status launch_variant(const CUtensorMap& tq, const CUtensorMap& tk, const CUt
                          const TcArgs& a, int64_t grid, cudaStream_t st) {
   auto kern = fwd_tc_kernel<D, BF16, MASK, MaskT>;
   constexpr int smem = TcCfg<D>::kSmemBytes;
-  PA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  static uint64_t attr_set = 0;  // one bit per device
+  PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, &attr_set));
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(tq, tk, tv, a);
   PA_CUDA(cudaGetLastError());
   return PA_OK;
