@@ -117,6 +117,8 @@ pa_status pa_stream_sync(void* stream);
 pa_status pa_event_create(void** event);
 pa_status pa_event_destroy(void* event);
 pa_status pa_event_record(void* event, void* stream);
+/* Make later work on `stream` wait for `event` (cross-stream ordering). */
+pa_status pa_stream_wait_event(void* stream, void* event);
 pa_status pa_event_elapsed_ms(void* start, void* stop, float* ms);
 
 /* ---- attention ---------------------------------------------------------- */

@@ -270,6 +270,11 @@ pa_status pa_event_record(void* event, void* stream) {
   return PA_OK;
 }
 
+pa_status pa_stream_wait_event(void* stream, void* event) {
+  PA_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0));
+  return PA_OK;
+}
+
 pa_status pa_event_elapsed_ms(void* start, void* stop, float* ms) {
   PA_CUDA(cudaEventSynchronize(static_cast<cudaEvent_t>(stop)));
   PA_CUDA(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start),

@@ -55,12 +55,15 @@ struct TcCfg {
   static constexpr int kBoxes = D / 64;
   static constexpr int kQBytes = BM * D * 2;
   static constexpr int kTileBytes = BN * D * 2;
-  static constexpr int kStages = (D == 128) ? 2 : 3;
+  // V of key tile i stays in use until tile 1's PV, issued one iteration
+  // later than tile 0's, so V gets one more stage than K.
+  static constexpr int kKStages = (D == 128) ? 2 : 3;
+  static constexpr int kVStages = (D == 128) ? 3 : 4;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kTiles * kQBytes;
-  static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
-  static constexpr int kNumBars = 1 + 4 * kStages + 3 * kTiles + 1;
+  static constexpr int kVOff = kKOff + kKStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 3 * kTiles + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
   static constexpr uint32_t col_s(int t) { return 128u * t; }
@@ -175,10 +178,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + C::kStages;
-  uint64_t* v_full = k_empty + C::kStages;
-  uint64_t* v_empty = v_full + C::kStages;
-  uint64_t* s_full = v_empty + C::kStages;  // [kTiles]
+  uint64_t* k_empty = k_full + C::kKStages;
+  uint64_t* v_full = k_empty + C::kKStages;
+  uint64_t* v_empty = v_full + C::kVStages;
+  uint64_t* s_full = v_empty + C::kVStages;  // [kTiles]
   uint64_t* p_full = s_full + kTiles;       // [kTiles]
   uint64_t* o_done = p_full + kTiles;       // [kTiles]
   uint64_t* mma_done = o_done + kTiles;
@@ -242,9 +245,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < C::kStages; ++s) {
+    for (int s = 0; s < C::kKStages; ++s) {
       mbar_init(k_full + s, 1);
       mbar_init(k_empty + s, 1);
+    }
+    for (int s = 0; s < C::kVStages; ++s) {
       mbar_init(v_full + s, 1);
       mbar_init(v_empty + s, 1);
     }
@@ -277,32 +282,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int b = 0; b < C::kBoxes; ++b)
           tma_load_3d(sQ + t * C::kQBytes + b * (BM * 128), &tq, q_full, b * 64,
                       static_cast<int32_t>(m0 + t * BM), zq);
-      int last_k[C::kStages], last_v[C::kStages];
+      int last_k[C::kKStages], last_v[C::kVStages];
 #pragma unroll
-      for (int s = 0; s < C::kStages; ++s) last_k[s] = last_v[s] = -1;
+      for (int s = 0; s < C::kKStages; ++s) last_k[s] = -1;
+#pragma unroll
+      for (int s = 0; s < C::kVStages; ++s) last_v[s] = -1;
       int i = 0;
       for (int j = 0; j < n_blocks; ++j) {
         if (!block_live(j)) continue;
-        const int st = i % C::kStages;
-        const uint32_t ph = (i / C::kStages) & 1;
-        if (!mbar_wait(k_empty + st, ph ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
-        mbar_expect_tx(k_full + st, C::kTileBytes);
+        const int ks = i % C::kKStages, vs = i % C::kVStages;
+        if (!mbar_wait(k_empty + ks, ((i / C::kKStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
+        mbar_expect_tx(k_full + ks, C::kTileBytes);
         for (int b = 0; b < C::kBoxes; ++b)
-          tma_load_3d(sK + st * C::kTileBytes + b * (BN * 128), &tk, k_full + st, b * 64, j * BN, zkv);
-        last_k[st] = i;
-        if (!mbar_wait(v_empty + st, ph ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
-        mbar_expect_tx(v_full + st, C::kTileBytes);
+          tma_load_3d(sK + ks * C::kTileBytes + b * (BN * 128), &tk, k_full + ks, b * 64, j * BN, zkv);
+        last_k[ks] = i;
+        if (!mbar_wait(v_empty + vs, ((i / C::kVStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
+        mbar_expect_tx(v_full + vs, C::kTileBytes);
         for (int b = 0; b < C::kBoxes; ++b)
-          tma_load_3d(sV + st * C::kTileBytes + b * (BN * 128), &tv, v_full + st, b * 64, j * BN, zkv);
-        last_v[st] = i;
+          tma_load_3d(sV + vs * C::kTileBytes + b * (BN * 128), &tv, v_full + vs, b * 64, j * BN, zkv);
+        last_v[vs] = i;
         ++i;
       }
       mbar_drain(q_full, 0);
 #pragma unroll
-      for (int s = 0; s < C::kStages; ++s) {
-        if (last_k[s] >= 0) mbar_drain(k_full + s, (last_k[s] / C::kStages) & 1);
-        if (last_v[s] >= 0) mbar_drain(v_full + s, (last_v[s] / C::kStages) & 1);
-      }
+      for (int s = 0; s < C::kKStages; ++s)
+        if (last_k[s] >= 0) mbar_drain(k_full + s, (last_k[s] / C::kKStages) & 1);
+#pragma unroll
+      for (int s = 0; s < C::kVStages; ++s)
+        if (last_v[s] >= 0) mbar_drain(v_full + s, (last_v[s] / C::kVStages) & 1);
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -329,9 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++cnt[t];
       };
       auto issue_pv = [&](int t, int i, bool release_v) -> bool {
-        const int st = i % C::kStages;
+        const int st = i % C::kVStages;
         if (!mbar_wait(p_full + t, pv_cnt[t] & 1, a.status, kStatusTimeoutSoftmax, abort_flag)) return false;
-        if (!mbar_wait(v_full + st, (i / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
+        if (!mbar_wait(v_full + st, (i / C::kVStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + st * C::kTileBytes);
 #pragma unroll
@@ -347,9 +354,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int i = 0;
       for (int j = 0; ok && j < n_blocks; ++j) {
         if (!block_live(j)) continue;
-        const int st = i % C::kStages;
+        const int st = i % C::kKStages;
         const bool live0 = tile_class(0, j) != 0, live1 = tile_class(1, j) != 0;
-        if (!mbar_wait(k_full + st, (i / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) {
+        if (!mbar_wait(k_full + st, (i / C::kKStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) {
           ok = false;
           break;
         }

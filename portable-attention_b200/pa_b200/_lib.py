@@ -102,6 +102,7 @@ SIGNATURES = {
     "pa_event_create": [ctypes.POINTER(_P)],
     "pa_event_destroy": [_P],
     "pa_event_record": [_P, _P],
+    "pa_stream_wait_event": [_P, _P],
     "pa_event_elapsed_ms": [_P, _P, ctypes.POINTER(ctypes.c_float)],
     "pa_sdpa_fwd": [_DESC, _P, _P, _P, _P, _P, _P, _P],
     "pa_decode_workspace_size": [_DESC, ctypes.POINTER(ctypes.c_size_t)],

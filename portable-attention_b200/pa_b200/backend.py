@@ -22,7 +22,7 @@ import threading
 import numpy as np
 
 from ._lib import PA_MASK_NONE, check, lib
-from .device import DeviceArena, Stream, sync_device_status
+from .device import DeviceArena, Event, Stream, pinned_empty, sync_device_status
 from .plan import plan_call
 from .validation import validate
 
@@ -80,9 +80,51 @@ def _dense_decode(plan) -> bool:
     return True
 
 
+_CHUNK_BYTES = 48 << 20   # target host<->device bytes per pipelined chunk
+_PIPELINE_MIN = 64 << 20  # below this a call is not worth splitting
+_PINNED_OUT_MIN = 1 << 20
+
+
+class _Pipes(threading.local):
+    """Per-thread streams for copy-in, compute and copy-out, and their events."""
+
+    def __init__(self):
+        self.h2d = self.d2h = None
+        self.events = []
+
+    def ensure(self, n_events):
+        if self.h2d is None:
+            self.h2d, self.d2h = Stream(), Stream()
+        while len(self.events) < n_events:
+            self.events.append((Event(), Event()))
+        return self.h2d, self.d2h, self.events[:n_events]
+
+
+_pipes = _Pipes()
+
+
+def _chunks(plan, host, out_nbytes):
+    """Split along leading dim 0 when every operand carries it densely."""
+    d = plan.desc
+    if not plan.out_lead or plan.out_lead[0] < 2:
+        return 1
+    if 0 in (d.q_lead_stride[0], d.k_lead_stride[0], d.v_lead_stride[0]):
+        return 1
+    total = sum(a.nbytes for a in host) + out_nbytes
+    if total < _PIPELINE_MIN:
+        return 1
+    return int(min(plan.out_lead[0], max(2, total // _CHUNK_BYTES)))
+
+
 def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p=0.0,
                                  is_causal=False, *, scale=None, enable_gqa=False):
-    """SDPA on the GPU with the reference backend contract; returns ``query.dtype``."""
+    """SDPA on the GPU with the reference backend contract; returns ``query.dtype``.
+
+    Large calls are cut along the first leading dimension and pipelined over
+    three streams, so the host->device copy of chunk c+1, the kernel of chunk
+    c and the device->host copy of chunk c-1 overlap; the result lands in a
+    page-locked array from the library's pool (plain NumPy array semantics).
+    """
     group = validate(query, key, value, attn_mask, dropout_p, is_causal, enable_gqa)
     plan = plan_call(query.shape, key.shape, value.shape, query.dtype, key.dtype, value.dtype,
                      None if attn_mask is None else np.shape(attn_mask),
@@ -94,28 +136,86 @@ def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p=0.
     if plan.mask_kind != PA_MASK_NONE:
         mask = np.ascontiguousarray(np.asarray(attn_mask).reshape(plan.mask_shape),
                                     dtype=plan.mask_host_dtype)
-    out = np.empty(plan.out_shape, dtype=cdt)
+    out_nbytes = int(np.prod(plan.out_shape)) * cdt.itemsize
+    if out_nbytes >= _PINNED_OUT_MIN:
+        out = pinned_empty(plan.out_shape, cdt)
+    else:
+        out = np.empty(plan.out_shape, dtype=cdt)
     if out.size == 0:
         return out.astype(query.dtype, copy=False)
     sizes = [a.nbytes for a in host] + [mask.nbytes if mask is not None else 0, out.nbytes]
     st = _stream()
     L = lib()
+    decode = use_decode_kernel(plan)
+    n_chunks = 1 if decode else _chunks(plan, host, out.nbytes)
     arena = _arena()
     with arena.lock:
         dq, dk, dv, dm, do = arena.carve(sizes)
-        for dptr, a in zip((dq, dk, dv), host):
-            check(L.pa_memcpy_h2d(dptr, a.ctypes.data, a.nbytes, st.handle))
-        if mask is not None:
-            check(L.pa_memcpy_h2d(dm, mask.ctypes.data, mask.nbytes, st.handle))
-        if use_decode_kernel(plan):
-            check(L.pa_decode_fwd(ctypes.byref(plan.desc), dq, dk, dv, do, None, None, 0, st.handle))
+        if n_chunks == 1:
+            for dptr, a in zip((dq, dk, dv), host):
+                check(L.pa_memcpy_h2d(dptr, a.ctypes.data, a.nbytes, st.handle))
+            if mask is not None:
+                check(L.pa_memcpy_h2d(dm, mask.ctypes.data, mask.nbytes, st.handle))
+            if decode:
+                check(L.pa_decode_fwd(ctypes.byref(plan.desc), dq, dk, dv, do, None, None, 0,
+                                      st.handle))
+            else:
+                check(L.pa_sdpa_fwd(ctypes.byref(plan.desc), dq, dk, dv,
+                                    dm if mask is not None else None, do, None, st.handle))
+            check(L.pa_memcpy_d2h(out.ctypes.data, do, out.nbytes, st.handle))
+            st.synchronize()
         else:
-            check(L.pa_sdpa_fwd(ctypes.byref(plan.desc), dq, dk, dv, dm if mask is not None else None,
-                                do, None, st.handle))
-        check(L.pa_memcpy_d2h(out.ctypes.data, do, out.nbytes, st.handle))
-        st.synchronize()
+            _run_pipelined(plan, host, mask, out, (dq, dk, dv, dm, do), n_chunks, query, key,
+                           value, attn_mask, is_causal, scale, group, st)
     sync_device_status()
     return out.astype(query.dtype, copy=False)
+
+
+def _run_pipelined(plan, host, mask, out, ptrs, n_chunks, query, key, value, attn_mask,
+                   is_causal, scale, group, st):
+    """Copy-in / compute / copy-out of batch chunks on three overlapping streams."""
+    L = lib()
+    h2d, d2h, events = _pipes.ensure(n_chunks)
+    dq, dk, dv, dm, do = ptrs
+    B = plan.out_lead[0]
+    bounds = [(B * c) // n_chunks for c in range(n_chunks + 1)]
+    per = [a.nbytes // B for a in host]
+    out_per = out.nbytes // B
+    mask_split = mask is not None and plan.desc.m_lead_stride[0] != 0
+    mask_per = mask.nbytes // B if mask_split else 0
+    if mask is not None and not mask_split:
+        check(L.pa_memcpy_h2d(dm, mask.ctypes.data, mask.nbytes, h2d.handle))
+    ready = Event()
+    ready.record(st)        # the arena's previous users are done with these buffers
+    ready.wait_on(h2d)
+    for c in range(n_chunks):
+        b0, b1 = bounds[c], bounds[c + 1]
+        loaded, computed = events[c]
+        for dptr, a, n in zip((dq, dk, dv), host, per):
+            check(L.pa_memcpy_h2d(dptr + b0 * n, a.ctypes.data + b0 * n, (b1 - b0) * n, h2d.handle))
+        if mask_split:
+            check(L.pa_memcpy_h2d(dm + b0 * mask_per, mask.ctypes.data + b0 * mask_per,
+                                  (b1 - b0) * mask_per, h2d.handle))
+        loaded.record(h2d)
+        loaded.wait_on(st)
+        shp = lambda x: (b1 - b0,) + tuple(np.shape(x))[1:]  # noqa: E731
+        m_shape = None
+        if mask is not None:
+            m_shape = shp(mask) if mask_split else mask.shape
+        sub = plan_call(shp(query), shp(key), shp(value), query.dtype, key.dtype, value.dtype,
+                        m_shape, None if mask is None else np.asarray(attn_mask).dtype,
+                        is_causal, scale, group)
+        m_ptr = None
+        if mask is not None:
+            m_ptr = dm + (b0 * mask_per if mask_split else 0)
+        check(L.pa_sdpa_fwd(ctypes.byref(sub.desc), dq + b0 * per[0], dk + b0 * per[1],
+                            dv + b0 * per[2], m_ptr, do + b0 * out_per, None, st.handle))
+        computed.record(st)
+        computed.wait_on(d2h)
+        check(L.pa_memcpy_d2h(out.ctypes.data + b0 * out_per, do + b0 * out_per,
+                              (b1 - b0) * out_per, d2h.handle))
+    d2h.synchronize()
+    st.synchronize()
 
 
 def sdpa_device(plan, q_ptr, k_ptr, v_ptr, out_ptr, *, mask_ptr=None, lse_ptr=None,

@@ -16,8 +16,8 @@ import numpy as np
 from ._lib import check, lib
 
 __all__ = [
-    "DeviceArena", "DeviceBuffer", "Event", "Stream", "current_device", "device_count",
-    "pinned_empty", "set_device", "sync_device_status",
+    "DeviceArena", "DeviceBuffer", "Event", "PinnedPool", "Stream", "current_device",
+    "device_count", "pinned_empty", "set_device", "sync_device_status",
 ]
 
 _ALIGN = 256
@@ -74,6 +74,10 @@ class Event:
     def record(self, stream: Stream | None = None) -> None:
         check(lib().pa_event_record(self.handle, stream.handle if stream else None))
 
+    def wait_on(self, stream: Stream) -> None:
+        """Make later work on ``stream`` wait until this event has completed."""
+        check(lib().pa_stream_wait_event(stream.handle, self.handle))
+
     def elapsed_ms(self, end: "Event") -> float:
         ms = ctypes.c_float(0.0)
         check(lib().pa_event_elapsed_ms(self.handle, end.handle, ctypes.byref(ms)))
@@ -123,24 +127,61 @@ class DeviceArena:
             self._buf = None
 
 
-class _PinnedOwner:
+class _PinnedBlock:
+    """One page-locked host allocation (freed when dropped by its pool)."""
+
     def __init__(self, nbytes: int) -> None:
         p = ctypes.c_void_p()
         check(lib().pa_host_alloc(ctypes.byref(p), max(int(nbytes), 1)))
         self.ptr = p.value
+        self.nbytes = int(nbytes)
         self._fin = weakref.finalize(self, lib().pa_host_free, p.value)
+
+
+class PinnedPool:
+    """Reuses page-locked host blocks: pinning is slow, so arrays handed out by
+    :meth:`array` give their block back to the pool (not to the OS) once the
+    array and every view of it are gone. At most ``cap`` bytes stay cached."""
+
+    GRANULE = 2 << 20
+
+    def __init__(self, cap: int = 8 << 30) -> None:
+        self._free: dict[int, list[_PinnedBlock]] = {}
+        self._cached = 0
+        self._cap = cap
+        self._lock = threading.Lock()
+
+    def array(self, shape, dtype) -> np.ndarray:
+        dt = np.dtype(dtype)
+        n = int(np.prod(shape)) * dt.itemsize
+        size = max(self.GRANULE, (n + self.GRANULE - 1) // self.GRANULE * self.GRANULE)
+        with self._lock:
+            bucket = self._free.get(size)
+            block = bucket.pop() if bucket else None
+            if block is not None:
+                self._cached -= size
+        if block is None:
+            block = _PinnedBlock(size)
+        raw = (ctypes.c_byte * max(n, 1)).from_address(block.ptr)
+        weakref.finalize(raw, self._give_back, block)
+        return np.frombuffer(raw, dtype=np.uint8, count=n).view(dt).reshape(shape)
+
+    def _give_back(self, block: _PinnedBlock) -> None:
+        with self._lock:
+            if self._cached + block.nbytes <= self._cap:
+                self._free.setdefault(block.nbytes, []).append(block)
+                self._cached += block.nbytes
+                return
+        block._fin()
+
+
+_pool = PinnedPool()
 
 
 def pinned_empty(shape, dtype) -> np.ndarray:
     """An uninitialised NumPy array in page-locked host memory (fast H2D/D2H).
 
-    The memory is released when the array (and every view of it) is gone.
+    The block returns to a process-wide pool when the array (and every view
+    of it) is gone, so repeated calls of the same size do not re-pin memory.
     """
-    dt = np.dtype(dtype)
-    n = int(np.prod(shape)) * dt.itemsize
-    owner = _PinnedOwner(n)
-    raw = (ctypes.c_byte * max(n, 1)).from_address(owner.ptr)
-    arr = np.frombuffer(raw, dtype=np.uint8, count=n).view(dt).reshape(shape)
-    # Keep the owner alive as long as the ctypes buffer backing the array.
-    raw._pa_owner = owner  # type: ignore[attr-defined]
-    return arr
+    return _pool.array(shape, dtype)
