@@ -448,9 +448,12 @@ def run_gpu(args):
             return pa_b200.sdpa_backward(host["q"], host["k"], host["v"], host["dout"], **kw)
         return (pa_b200.scaled_dot_product_attention(host["q"], host["k"], host["v"], **kw),)
 
-    for _ in range(max(1, min(args.warmup, 2))):
-        public_call()
-    e2e_steps = max(1, min(args.steps, 5))
+    # Warm up exactly like the timed loop (the previous result stays alive while
+    # the next call runs), so the pinned-output pool reaches its steady state.
+    res = None
+    for _ in range(3):
+        res = public_call()
+    e2e_steps = max(1, min(args.steps, 10))
     barrier(pg)
     t0 = time.perf_counter()
     for _ in range(e2e_steps):

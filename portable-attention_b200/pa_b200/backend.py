@@ -134,8 +134,11 @@ def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p=0.
     host = [np.ascontiguousarray(x, dtype=cdt) for x in (query, key, value)]
     mask = None
     if plan.mask_kind != PA_MASK_NONE:
-        mask = np.ascontiguousarray(np.asarray(attn_mask).reshape(plan.mask_shape),
-                                    dtype=plan.mask_host_dtype)
+        m = np.asarray(attn_mask).reshape(plan.mask_shape)
+        if m.dtype == np.bool_:
+            mask = np.ascontiguousarray(m).view(np.uint8)  # same bytes, no conversion copy
+        else:
+            mask = np.ascontiguousarray(m, dtype=plan.mask_host_dtype)
     out_nbytes = int(np.prod(plan.out_shape)) * cdt.itemsize
     if out_nbytes >= _PINNED_OUT_MIN:
         out = pinned_empty(plan.out_shape, cdt)
