@@ -63,7 +63,7 @@ struct TcCfg {
   static constexpr int kKOff = kTiles * kQBytes;
   static constexpr int kVOff = kKOff + kKStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
-  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 3 * kTiles + 1;
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 3 * kTiles + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
   static constexpr uint32_t col_s(int t) { return 128u * t; }
@@ -79,7 +79,7 @@ struct TcArgs {
   LeadTable mlt;        // mask element offsets per output slice
   int64_t L, S;
   int64_t m_rs, m_cs;
-  int64_t slices;
+  int64_t slices, items;
   int32_t H, Hkv, group, pairs;
   int32_t row_tiles, col_blocks;
   int32_t causal;
@@ -185,42 +185,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + kTiles;       // [kTiles]
   uint64_t* o_done = p_full + kTiles;       // [kTiles]
   uint64_t* mma_done = o_done + kTiles;
+  uint64_t* q_empty = mma_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item: groups of kGroupSlices heads (which share K/V under GQA) run
-  // together, heaviest query-tile pairs of the group first.
-  int64_t slice;
-  int pair;
-  {
-    const int64_t item = blockIdx.x;
+  // Persistent CTAs: CTA c takes work items c, c + gridDim.x, ... A work item
+  // is (query-tile pair, slice); items of kGroupSlices heads (which share K/V
+  // under GQA) are consecutive, heaviest query-tile pairs of a group first, so
+  // the CTAs running at any moment share K/V in L2.
+  int64_t slice = 0, m0 = 0;
+  int32_t zq = 0, zkv = 0;
+  int n_blocks = 0;
+  const uint8_t* cls_row[kTiles] = {nullptr, nullptr};
+  auto set_item = [&](int64_t item) {
     const int64_t per_group = static_cast<int64_t>(kGroupSlices) * a.pairs;
     const int64_t g = item / per_group;
     const int64_t g0 = g * kGroupSlices;
     const int64_t gsz = (a.slices - g0 < kGroupSlices) ? a.slices - g0 : kGroupSlices;
     const int64_t rem = item - g * per_group;
-    pair = a.pairs - 1 - static_cast<int>(rem / gsz);
+    const int pair = a.pairs - 1 - static_cast<int>(rem / gsz);
     slice = g0 + rem % gsz;
-  }
-  const int64_t m0 = static_cast<int64_t>(pair) * (kTiles * BM);
-  const int32_t zq = static_cast<int32_t>(slice);
-  const int32_t zkv = static_cast<int32_t>((slice / a.H) * a.Hkv + (slice % a.H) / a.group);
-  const int64_t last_row = (m0 + kTiles * BM < a.L ? m0 + kTiles * BM : a.L) - 1;
-  int64_t kv_end = a.S;
-  if (a.causal) kv_end = last_row + 1 < a.S ? last_row + 1 : a.S;
-  const int n_blocks = static_cast<int>((kv_end + BN - 1) / BN);
-  const uint8_t* cls_row[kTiles] = {nullptr, nullptr};
-  if (MASK == PA_MASK_BOOL && a.mcls) {
-    const int64_t ms = mask_slice_id(a.mlt, slice);
+    m0 = static_cast<int64_t>(pair) * (kTiles * BM);
+    zq = static_cast<int32_t>(slice);
+    zkv = static_cast<int32_t>((slice / a.H) * a.Hkv + (slice % a.H) / a.group);
+    const int64_t last_row = (m0 + kTiles * BM < a.L ? m0 + kTiles * BM : a.L) - 1;
+    int64_t kv_end = a.S;
+    if (a.causal) kv_end = last_row + 1 < a.S ? last_row + 1 : a.S;
+    n_blocks = static_cast<int>((kv_end + BN - 1) / BN);
+    cls_row[0] = cls_row[1] = nullptr;
+    if (MASK == PA_MASK_BOOL && a.mcls) {
+      const int64_t ms = mask_slice_id(a.mlt, slice);
 #pragma unroll
-    for (int t = 0; t < kTiles; ++t) {
-      const int64_t rt = (m0 / BM) + t;
-      cls_row[t] = rt < a.row_tiles ? a.mcls + (ms * a.row_tiles + rt) * a.col_blocks : nullptr;
+      for (int t = 0; t < kTiles; ++t) {
+        const int64_t rt = (m0 / BM) + t;
+        cls_row[t] = rt < a.row_tiles ? a.mcls + (ms * a.row_tiles + rt) * a.col_blocks : nullptr;
+      }
     }
-  }
+  };
   // 0 dead, 1 full, 2 partial -- identical in every role.
   auto tile_class = [&](int t, int j) -> int {
     const int64_t r_lo = m0 + static_cast<int64_t>(t) * BM;
@@ -242,6 +246,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     return c;
   };
   auto block_live = [&](int j) -> bool { return tile_class(0, j) != 0 || tile_class(1, j) != 0; };
+  auto last_live = [&]() -> int {
+    for (int j = n_blocks - 1; j >= 0; --j)
+      if (block_live(j)) return j;
+    return -1;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -259,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(o_done + t, 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(q_empty, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -273,37 +283,51 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && n_blocks > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_expect_tx(q_full, kTiles * C::kQBytes);
-      for (int t = 0; t < kTiles; ++t)
-        for (int b = 0; b < C::kBoxes; ++b)
-          tma_load_3d(sQ + t * C::kQBytes + b * (BM * 128), &tq, q_full, b * 64,
-                      static_cast<int32_t>(m0 + t * BM), zq);
       int last_k[C::kKStages], last_v[C::kVStages];
 #pragma unroll
       for (int s = 0; s < C::kKStages; ++s) last_k[s] = -1;
 #pragma unroll
       for (int s = 0; s < C::kVStages; ++s) last_v[s] = -1;
-      int i = 0;
-      for (int j = 0; j < n_blocks; ++j) {
-        if (!block_live(j)) continue;
-        const int ks = i % C::kKStages, vs = i % C::kVStages;
-        if (!mbar_wait(k_empty + ks, ((i / C::kKStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
-        mbar_expect_tx(k_full + ks, C::kTileBytes);
-        for (int b = 0; b < C::kBoxes; ++b)
-          tma_load_3d(sK + ks * C::kTileBytes + b * (BN * 128), &tk, k_full + ks, b * 64, j * BN, zkv);
-        last_k[ks] = i;
-        if (!mbar_wait(v_empty + vs, ((i / C::kVStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
-        mbar_expect_tx(v_full + vs, C::kTileBytes);
-        for (int b = 0; b < C::kBoxes; ++b)
-          tma_load_3d(sV + vs * C::kTileBytes + b * (BN * 128), &tv, v_full + vs, b * 64, j * BN, zkv);
-        last_v[vs] = i;
-        ++i;
+      int it = 0, g = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+        set_item(item);
+        if (last_live() < 0) continue;
+        // Q of this item may overwrite the previous one once its S MMAs are done.
+        if (!mbar_wait(q_empty, (it & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
+        mbar_expect_tx(q_full, kTiles * C::kQBytes);
+        for (int t = 0; t < kTiles; ++t)
+          for (int b = 0; b < C::kBoxes; ++b)
+            tma_load_3d(sQ + t * C::kQBytes + b * (BM * 128), &tq, q_full, b * 64,
+                        static_cast<int32_t>(m0 + t * BM), zq);
+        ++it;
+        for (int j = 0; j < n_blocks; ++j) {
+          if (!block_live(j)) continue;
+          const int ks = g % C::kKStages, vs = g % C::kVStages;
+          if (!mbar_wait(k_empty + ks, ((g / C::kKStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(k_full + ks, C::kTileBytes);
+          for (int b = 0; b < C::kBoxes; ++b)
+            tma_load_3d(sK + ks * C::kTileBytes + b * (BN * 128), &tk, k_full + ks, b * 64, j * BN, zkv);
+          last_k[ks] = g;
+          if (!mbar_wait(v_empty + vs, ((g / C::kVStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(v_full + vs, C::kTileBytes);
+          for (int b = 0; b < C::kBoxes; ++b)
+            tma_load_3d(sV + vs * C::kTileBytes + b * (BN * 128), &tv, v_full + vs, b * 64, j * BN, zkv);
+          last_v[vs] = g;
+          ++g;
+        }
       }
-      mbar_drain(q_full, 0);
+      if (it > 0) mbar_drain(q_full, (it - 1) & 1);
 #pragma unroll
       for (int s = 0; s < C::kKStages; ++s)
         if (last_k[s] >= 0) mbar_drain(k_full + s, (last_k[s] / C::kKStages) & 1);
@@ -314,15 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA issue
-    if (lane == 0 && n_blocks > 0) {
+    if (lane == 0) {
       constexpr uint32_t idS = idesc_f16(BM, BN, false, false, BF16);
       constexpr uint32_t idO = idesc_f16(BM, D, false, true, BF16);
       const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait(q_full, 0, a.status, kStatusTimeoutLoad, abort_flag);
-      int cnt[kTiles] = {0, 0};   // S issued per tile
-      int pv_cnt[kTiles] = {0, 0};
-      int pend1 = -1;             // union index of tile 1's S awaiting its PV
-      bool pend1_solo = false;    // tile 0 was dead in that block (V release owed by tile 1)
+      int pv_cnt[kTiles] = {0, 0};   // PVs issued per tile over the CTA's life
+      bool first_pv[kTiles] = {true, true};
       auto issue_s = [&](int t, int st) {
         const uint32_t k_addr = smem_u32(sK + st * C::kTileBytes);
         const uint32_t qa = q_addr + t * C::kQBytes;
@@ -333,57 +354,70 @@ __global__ void __launch_bounds__(kThreads, 1)
                   sdesc_sw128(k_addr + box * (BN * 128) + sub, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
         tc_commit(s_full + t);
-        ++cnt[t];
       };
-      auto issue_pv = [&](int t, int i, bool release_v) -> bool {
-        const int st = i % C::kVStages;
+      auto issue_pv = [&](int t, int gi, bool release_v) -> bool {
+        const int st = gi % C::kVStages;
         if (!mbar_wait(p_full + t, pv_cnt[t] & 1, a.status, kStatusTimeoutSoftmax, abort_flag)) return false;
-        if (!mbar_wait(v_full + st, (i / C::kVStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
+        if (!mbar_wait(v_full + st, (gi / C::kVStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + st * C::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
           umma_ts(tmem + C::col_o(t), tmem + C::col_s(t) + kk * 8,
                   sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024), idO,
-                  (pv_cnt[t] > 0 || kk > 0) ? 1u : 0u);
+                  (!first_pv[t] || kk > 0) ? 1u : 0u);
         tc_commit(o_done + t);
         if (release_v) tc_commit(v_empty + st);
         ++pv_cnt[t];
+        first_pv[t] = false;
         return true;
       };
-      int i = 0;
-      for (int j = 0; ok && j < n_blocks; ++j) {
-        if (!block_live(j)) continue;
-        const int st = i % C::kKStages;
-        const bool live0 = tile_class(0, j) != 0, live1 = tile_class(1, j) != 0;
-        if (!mbar_wait(k_full + st, (i / C::kKStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) {
+      int it = 0, g = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+        set_item(item);
+        const int jl = last_live();
+        if (jl < 0) continue;
+        if (!mbar_wait(q_full, it & 1, a.status, kStatusTimeoutLoad, abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        if (live0) issue_s(0, st);
-        if (pend1 >= 0) {
-          // tile 1's previous block; its V stage is released here
-          if (!issue_pv(1, pend1, true)) {
+        ++it;
+        first_pv[0] = first_pv[1] = true;
+        int pend1 = -1;  // global index of tile 1's S awaiting its PV
+        for (int j = 0; j <= jl; ++j) {
+          if (!block_live(j)) continue;
+          const int st = g % C::kKStages;
+          const bool live0 = tile_class(0, j) != 0, live1 = tile_class(1, j) != 0;
+          if (!mbar_wait(k_full + st, (g / C::kKStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) {
             ok = false;
             break;
           }
-          pend1 = -1;
+          tc_fence_after();
+          if (live0) issue_s(0, st);
+          if (pend1 >= 0) {
+            // tile 1's previous block; its V stage is released here
+            if (!issue_pv(1, pend1, true)) {
+              ok = false;
+              break;
+            }
+            pend1 = -1;
+          }
+          if (live1) {
+            issue_s(1, st);
+            pend1 = g;
+          }
+          // Every S of this item is issued: its Q tiles may be replaced once they finish.
+          if (j == jl) tc_commit(q_empty);
+          tc_commit(k_empty + st);
+          if (live0 && !issue_pv(0, g, !live1)) {
+            ok = false;
+            break;
+          }
+          ++g;
         }
-        if (live1) {
-          issue_s(1, st);
-          pend1 = i;
-          pend1_solo = !live0;
-        }
-        tc_commit(k_empty + st);
-        if (live0 && !issue_pv(0, i, !live1)) {
-          ok = false;
-          break;
-        }
-        ++i;
+        if (ok && pend1 >= 0) ok = issue_pv(1, pend1, true);
       }
-      (void)pend1_solo;
-      if (ok && pend1 >= 0) issue_pv(1, pend1, true);
       tc_commit(mma_done);
       mbar_drain(mma_done, 0);
     }
@@ -393,16 +427,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = warp / 4;                 // query tile of this warpgroup
     const int quad = warp & 3;
     const int r = quad * 32 + lane;         // row inside the tile == TMEM lane
-    const int64_t row = m0 + static_cast<int64_t>(t) * BM + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t s_addr = lane_base + C::col_s(t);
     const uint32_t o_addr = lane_base + C::col_o(t);
-    const bool row_ok = row < a.L;
     const float sl2 = a.scale_log2;
+    int cnt = 0;  // softmax blocks of this tile over the CTA's life (barrier phases)
+    bool ok = true;
+    for (int64_t item = blockIdx.x; ok && item < a.items; item += gridDim.x) {
+    set_item(item);
+    const int64_t row = m0 + static_cast<int64_t>(t) * BM + r;
+    const bool row_ok = row < a.L;
     float m_run = -INFINITY, l_run = 0.f;
     const SliceOffsets moff = slice_offsets(a.mlt, slice);
-    int cnt = 0;
-    bool ok = true;
+    int icnt = 0;   // blocks of this item
 
     for (int j = 0; j < n_blocks; ++j) {
       const int cls = tile_class(t, j);
@@ -486,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       const float rowsum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       const float alpha = (m_use == m_run) ? 1.f : ((m_run == -INFINITY) ? 0.f : ex2(m_run - m_use));
-      const bool need = (cnt > 0) && (m_use != m_run);
+      const bool need = (icnt > 0) && (m_use != m_run);
       if (__any_sync(0xffffffffu, need)) {
         ok = mbar_wait(o_done + t, (cnt - 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
@@ -509,9 +546,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full + t);
       ++cnt;
+      ++icnt;
     }
 
-    if (ok && cnt > 0) {
+    if (ok && icnt > 0) {
       ok = mbar_wait(o_done + t, (cnt - 1) & 1, a.status, kStatusTimeoutMma, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
     }
@@ -522,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t rr[32];
-        if (cnt > 0) {
+        if (icnt > 0) {
           tmem_ld32(o_addr + c * 32, rr);
           tmem_ld_wait();
           reg_fence(rr);
@@ -543,8 +581,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (row_ok && a.lse)
         a.lse[slice * a.L + row] = l_run > 0.f ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
     }
+      }  // item loop
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -660,9 +698,9 @@ pa_status launch_fwd_tc(const pa_sdpa_desc& d, const void* q, const void* k, con
   a.causal = d.is_causal;
   a.scale_log2 = static_cast<float>(d.scale * 1.4426950408889634);
   a.inv_scale = static_cast<float>(1.0 / d.scale);
-  const int64_t grid = n * a.pairs;
-  if (grid == 0) return PA_OK;
-  if (grid > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "fwd_tc: grid too large");
+  a.items = n * a.pairs;
+  if (a.items == 0) return PA_OK;
+  const int64_t grid = a.items < sm_count() ? a.items : sm_count();
   uint8_t* cls = nullptr;
   if (!d.is_causal && d.mask_kind == PA_MASK_BOOL) {
     const int64_t tiles = mask_slice_count(a.mlt) * a.row_tiles * a.col_blocks;
