@@ -40,8 +40,10 @@ enum {
   PA_ERR_NOMEM = 6        /* device or pinned-host allocation failed */
 };
 
-/* Element types. */
-enum { PA_F16 = 1, PA_BF16 = 2, PA_F32 = 3, PA_F64 = 4, PA_BOOL = 5 };
+/* Element types. PA_FP8_E4M3 is the OCP FP8 E4M3 format ("e4m3fn": 1 sign,
+ * 4 exponent bits with bias 7, 3 mantissa bits, no infinities, 0x7f / 0xff
+ * NaN, largest finite 448); it is accepted only as a decode cache type. */
+enum { PA_F16 = 1, PA_BF16 = 2, PA_F32 = 3, PA_F64 = 4, PA_BOOL = 5, PA_FP8_E4M3 = 6 };
 
 /* Mask kinds: none, boolean keep-mask (1 byte per element, nonzero = keep),
  * additive float mask (type mask_dtype) added to the scaled scores. */
@@ -153,6 +155,73 @@ pa_status pa_decode_workspace_size(const pa_sdpa_desc* desc, size_t* bytes);
 pa_status pa_decode_fwd(const pa_sdpa_desc* desc, const void* q, const void* k, const void* v,
                         void* out, float* lse, void* workspace, size_t workspace_bytes,
                         void* stream);
+
+/*
+ * Decode over a key/value cache: the L == 1 attention of pa_decode_fwd for a
+ * batch of sequences with their own lengths, read from a contiguous or a
+ * paged cache in fp16, bf16 or fp8 e4m3. No reference counterpart: the
+ * reference's interface takes dense key/value tensors only
+ * (dispatch.py:53-76); this is its math (reference.py:139-162) per sequence
+ * over keys [0, seq_lens[b]) of that sequence.
+ *
+ * Cache layout. Keys and values live in pages of `page_size` keys; element
+ * (page, kv head h, key row r, column d) is at
+ *   page * page_stride + h * head_stride + r * key_stride + d
+ * elements from the cache base (k and v share the layout), so both
+ * (pages, kv_heads, page_size, D) and (pages, page_size, kv_heads, D) caches
+ * are accepted as they are. Byte strides must be multiples of 16 and the
+ * bases 16-byte aligned.
+ *   With a block table (int32 [batch][max_pages_per_seq], device memory):
+ *   key j of sequence b is row j % page_size of page
+ *   block_table[b][j / page_size]; page_size is a multiple of 8. Entries past
+ *   a sequence's last page are not read.
+ *   Without one (NULL): page b holds sequence b from row 0, so a dense
+ *   (batch, kv_heads, S, D) cache is page_size = S, num_pages = batch.
+ * seq_lens (int32 [batch], device memory) gives each sequence's length, at
+ * most max_seq_len; NULL means every sequence holds max_seq_len keys. A
+ * sequence of length 0 gets a zero output row and lse = -inf. Cache rows past
+ * a sequence's length are never used, whatever they hold.
+ *
+ * q and out are dense (batch, q_heads, head_dim) in q_dtype; lse (optional)
+ * is float32 (batch, q_heads), natural log. Grouped-query attention shares
+ * kv head h among q heads [h*G, (h+1)*G), G = q_heads / kv_heads in
+ * {1, 2, 4, 8}; head_dim is 64 or 128.
+ *
+ * fp8 caches: scores use k * k_scale and the output v * v_scale (per-tensor
+ * dequantisation); set both to 1.0 for fp16/bf16 caches. `scale` is the
+ * softmax scale (1/sqrt(head_dim) for the reference's default).
+ *
+ * A sequence length outside [0, max_seq_len] or a block-table entry outside
+ * [0, num_pages) is detected on the device: the keys involved are treated
+ * as zeros and pa_device_status() then reports PA_ERR_INVALID (codes 0x201
+ * and 0x202); no out-of-bounds memory is read.
+ *
+ * `workspace` as for pa_decode_fwd (NULL: stream-ordered pool), at least
+ * pa_decode_kv_workspace_size() bytes; `paged` is nonzero when a block table
+ * will be passed.
+ */
+typedef struct pa_kv_cache_desc {
+  int32_t q_dtype;            /* PA_F16 / PA_BF16: q and out */
+  int32_t kv_dtype;           /* q_dtype, or PA_FP8_E4M3 */
+  int64_t batch;              /* sequences, one query row each */
+  int64_t q_heads, kv_heads;
+  int64_t head_dim;           /* 64 or 128 */
+  int64_t max_seq_len;        /* bound on every seq_lens[b]; sizes the key split */
+  int64_t page_size;          /* keys per page */
+  int64_t num_pages;          /* pages in the cache */
+  int64_t max_pages_per_seq;  /* block-table row length (ignored without one) */
+  int64_t key_stride;         /* elements between consecutive keys (rows) */
+  int64_t head_stride;        /* elements between kv heads */
+  int64_t page_stride;        /* elements between pages */
+  double scale;               /* softmax scale */
+  float k_scale, v_scale;     /* dequantisation factors (1.0 unless fp8) */
+} pa_kv_cache_desc;
+
+pa_status pa_decode_kv_workspace_size(const pa_kv_cache_desc* desc, int32_t paged, size_t* bytes);
+pa_status pa_decode_kv_fwd(const pa_kv_cache_desc* desc, const void* q, const void* k_cache,
+                           const void* v_cache, const int32_t* block_table,
+                           const int32_t* seq_lens, void* out, float* lse, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /*
  * Allocation-free variant of pa_decode_fwd. It has no counterpart in the

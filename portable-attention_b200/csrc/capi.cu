@@ -104,28 +104,61 @@ void scratch_free(void* p, cudaStream_t s) {
   if (p) cudaFreeAsync(p, s);
 }
 
+namespace {
+pa_status encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+      cudaGetLastError();
+      return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  *out = g_encode;
+  return PA_OK;
+}
+}  // namespace
+
+pa_status encode_tma_4d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
+                        const uint64_t dims[4], const uint64_t strides_bytes[3],
+                        uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  PA_TRY(encoder(&enc));
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t st[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t box[4] = {box_inner, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, const_cast<void*>(base), d, st, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[320];
+    snprintf(buf, sizeof buf,
+             "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu x %llu x %llu, byte strides "
+             "%llu/%llu/%llu, box %u x %u (strides must be multiples of 16 bytes and the base "
+             "16-byte aligned)",
+             static_cast<int>(r), (unsigned long long)dims[0], (unsigned long long)dims[1],
+             (unsigned long long)dims[2], (unsigned long long)dims[3],
+             (unsigned long long)strides_bytes[0], (unsigned long long)strides_bytes[1],
+             (unsigned long long)strides_bytes[2], box_inner, box_rows);
+    return fail(PA_ERR_INVALID, buf);
+  }
+  return PA_OK;
+}
+
 pa_status encode_tma_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
                         uint64_t inner, uint64_t rows, uint64_t planes, uint64_t row_bytes,
                         uint64_t plane_bytes, uint32_t box_inner, uint32_t box_rows,
                         CUtensorMapSwizzle swz) {
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_encode) {
-      void* fn = nullptr;
-      cudaDriverEntryPointQueryResult q{};
-      cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
-        cudaGetLastError();
-        return fail(PA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-      }
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
-  }
+  PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  PA_TRY(encoder(&enc));
   cuuint64_t dims[3] = {inner, rows, planes};
   cuuint64_t strides[2] = {row_bytes, plane_bytes};
   cuuint32_t box[3] = {box_inner, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -181,8 +214,13 @@ pa_status pa_device_status(int32_t* code) {
   if (code) *code = v;
   if (v) {
     char buf[96];
-    snprintf(buf, sizeof buf, "a bounded device-side wait gave up (code 0x%x)", v);
-    return fail(PA_ERR_TIMEOUT, buf);
+    if (v == kStatusBadSeqLen)
+      snprintf(buf, sizeof buf, "a sequence length was outside [0, max_seq_len] (code 0x%x)", v);
+    else if (v == kStatusBadPage)
+      snprintf(buf, sizeof buf, "a block-table entry was outside [0, num_pages) (code 0x%x)", v);
+    else
+      snprintf(buf, sizeof buf, "a bounded device-side wait gave up (code 0x%x)", v);
+    return fail((v & 0xf00) == 0x200 ? PA_ERR_INVALID : PA_ERR_TIMEOUT, buf);
   }
   return PA_OK;
 }

@@ -55,6 +55,13 @@ pa_status encode_tma_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* ba
                         uint64_t plane_bytes, uint32_t box_inner, uint32_t box_rows,
                         CUtensorMapSwizzle swz);
 
+// 4-D map [inner, rows, heads, pages] with byte strides for the three outer
+// dimensions; box = (box_inner, box_rows, 1, 1). Used for key/value caches
+// that are either dense (batch, heads, keys, D) or split into pages.
+pa_status encode_tma_4d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
+                        const uint64_t dims[4], const uint64_t strides_bytes[3],
+                        uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz);
+
 // ------------------------------------------------------- descriptor helpers
 
 inline int64_t lead_count(const pa_sdpa_desc& d) {
@@ -122,6 +129,8 @@ enum : int {
   kStatusTimeoutMma = 0x102,    // waiting for a tensor-core result
   kStatusTimeoutSoftmax = 0x103,
   kStatusTimeoutFree = 0x104,   // producer waiting for a free stage
+  kStatusBadSeqLen = 0x201,     // a sequence length outside [0, max_seq_len]
+  kStatusBadPage = 0x202,       // a block-table entry outside [0, num_pages)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -206,6 +215,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 

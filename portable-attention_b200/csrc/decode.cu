@@ -1,28 +1,48 @@
-// Split-KV decode forward (query length 1), HBM-bound, on CUDA cores.
+// Split-KV decode forward (query length 1), HBM-bound.
 //
-// Work unit: (batch b, key/value head kh, split s) -> one CTA that reads keys
-// [s*chunk, min(S, (s+1)*chunk)) of K[b, kh] and V[b, kh] exactly once and
-// serves all G = Hq / Hkv query heads that share that key/value head, so
-// grouped-query K/V is never repeated.
+// Work unit: (sequence b, key/value head kh, split s) -> one CTA that reads
+// keys [s*chunk, min(len_b, (s+1)*chunk)) of K[b, kh] and V[b, kh] exactly
+// once and serves all G = Hq / Hkv query heads that share that key/value
+// head, so grouped-query K/V is never repeated.
+//
+// One kernel serves three cache layouts through a 4-D tensor map
+// [D, page rows, kv heads, pages] with arbitrary strides:
+//   dense     (B, Hkv, S, D), the reference's operand layout: page b holds
+//             sequence b (pa_decode_fwd);
+//   varlen    the same with a length per sequence (seq_lens);
+//   paged     pages of `page_size` keys named by a block table, in any
+//             (page, head, key) stride order, e.g. (pages, Hkv, page, D) or
+//             (pages, page, Hkv, D).
+// Key/value elements are fp16, bf16 (the query's type) or fp8 e4m3 with
+// per-tensor dequantisation scales: k_scale folds into the softmax scale and
+// v_scale into the final normalisation.
 //
 // CTA = 1 producer warp + 8 compute warps.
-//   producer  TMA-loads 32-key K and V tiles (128-byte swizzle, 64-column
-//             boxes) into a ring of shared-memory stages; keeps ~190 KB in
-//             flight per SM so HBM stays busy.
-//   compute   warp w consumes tiles w, w+8, w+16, ... on its own:
-//               scores   lane j <-> key j of the tile; q (fp32, G heads) is
-//                        read from shared memory as broadcasts, the key row
-//                        with conflict-free 16-byte loads (swizzled);
-//               softmax  per-head running max / sum in log2 units;
-//               P V      lane l <-> value columns [l*D/32, (l+1)*D/32), the
-//                        probabilities of the 32 keys broadcast by shuffles.
+//   producer  TMA-loads 32-key K and V tiles (128-byte swizzle, or 64-byte for
+//             64-byte rows) into a ring of shared-memory stages (a multiple
+//             of 8 stages, so each stage always serves the same compute
+//             warp); keeps up to 192 KB in flight per SM so HBM stays busy. For a paged cache it
+//             stages the block table in shared memory 32 entries at a time,
+//             one window ahead (cp.async), and splits a tile into 16- or 8-row
+//             pieces when pages are shorter than 32 keys.
+//   compute   warp w consumes tiles w, w+8, w+16, ... on its own, on tensor
+//             cores (warp-level m16n8k16, fp32 accumulators): S = Q K^T for
+//             the G query heads (zero-padded to 16 rows), online softmax on
+//             the accumulators, O^T += V^T P^T with P straight from those
+//             accumulators. fp8 tiles are converted to f16 in registers.
+//             Keys past the sequence end are masked and their value rows
+//             zeroed, so stale cache contents (even NaN) never reach the
+//             output.
 //             The 8 warps' partial states merge in shared memory at the end
 //             and the CTA writes one partial (m, l, acc[D]) per query head
 //             into the workspace.
 // combine     one CTA per (b, query head) merges the splits by log-sum-exp
-//             and writes the fp16/bf16 output and, optionally, the lse.
+//             and writes the fp16/bf16 output and, optionally, the lse. A
+//             sequence with no keys gets a zero output and lse = -inf.
 //
-// The math is reference.py:139-162 for L == 1 (no mask, not causal).
+// The math is reference.py:139-162 for L == 1 (no mask, not causal), per
+// sequence over its own keys.
+#include <cuda_fp8.h>
 #include <math.h>
 
 #include <cmath>
@@ -41,16 +61,40 @@ constexpr int kThreadsDec = 32 * (kWarpsC + 1);
 constexpr int kTileKeys = 32;
 constexpr float kLn2f = 0.6931471805599453f;
 
-template <int D>
+enum : int { kKvF16 = 0, kKvBF16 = 1, kKvE4M3 = 2 };
+
+template <int D, int KV>
 struct DecCfg {
-  static constexpr int kBoxes = D / 64;
-  static constexpr int kTileBytes = kTileKeys * D * 2;        // one K (or V) tile
-  static constexpr int kStageBytes = 2 * kTileBytes;          // K + V
-  static constexpr int kStages = D == 128 ? 12 : 20;
+  static constexpr int kEsz = KV == kKvE4M3 ? 1 : 2;
+  static constexpr int kRowBytes = D * kEsz;                        // one key row
+  static constexpr int kBoxBytes = kRowBytes < 128 ? kRowBytes : 128;  // 128 (SW128) or 64 (SW64)
+  static constexpr int kBoxCols = kBoxBytes / kEsz;
+  static constexpr int kBoxes = kRowBytes / kBoxBytes;
+  static constexpr int kTileBytes = kTileKeys * kRowBytes;          // one K (or V) tile
+  static constexpr int kStageBytes = 2 * kTileBytes;                // K + V
+  // Tile t lives in stage t % kStages and is consumed by warp t % kWarpsC.
+  // With kStages a multiple of kWarpsC every stage belongs to one warp, so a
+  // warp waiting for tile t has itself consumed the stage's previous tile
+  // t - kStages: its barrier wait can never be two phases ahead (a parity wait
+  // two phases ahead would pass on the older phase and read a tile still in
+  // flight). Up to 192 KB of stages.
+  static constexpr int kStages = (196608 / kStageBytes) / kWarpsC * kWarpsC;
+  static_assert(kStages % kWarpsC == 0 && kStages >= kWarpsC, "stage ownership");
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kQOff = kRingBytes;                    // G*D floats (G <= 8)
+  static constexpr int kQOff = kRingBytes;                          // G*D floats (G <= 8)
   static constexpr int kBarOff = kQOff + 8 * D * 4;
-  static constexpr int kSmemBytes = kBarOff + 2 * kStages * 8 + 16 + 1024;
+  static constexpr int kBtOff = kBarOff + 2 * kStages * 8 + 16;     // 2 x 32 block-table entries
+  static constexpr int kSmemBytes = kBtOff + 256 + 1024;
+
+  // Byte offset of byte `byte` of key row `row` inside a tile: 64-column
+  // (128-byte) boxes one after another, rows 128 (or 64) bytes apart, the
+  // 16-byte chunks permuted by the TMA swizzle (128B: chunk ^= row % 8;
+  // 64B: chunk ^= (row / 2) % 4).
+  static __device__ __forceinline__ int off(int row, int byte) {
+    const int bx = byte / kBoxBytes, b = byte % kBoxBytes;
+    const int sw = kBoxBytes == 128 ? (row & 7) : ((row >> 1) & 3);
+    return bx * (kTileKeys * kBoxBytes) + row * kBoxBytes + (((b >> 4) ^ sw) << 4) + (b & 15);
+  }
 };
 
 struct DecArgs {
@@ -58,40 +102,89 @@ struct DecArgs {
   float* ws_acc;   // [B*Hq][nsplit][D]
   float* ws_ml;    // [B*Hq][nsplit][2]  (m in log2 units, l)
   int* status;
-  int64_t S;
+  const int32_t* block_table;  // [B][max_pages] or null (page b = sequence b)
+  const int32_t* seq_lens;     // [B] or null (every sequence holds S keys)
+  int64_t S;                   // bound on every sequence length
+  int64_t max_pages;
   int32_t Hq, Hkv, nsplit, chunk;
-  float scale_log2;
+  int32_t page_size, piece_rows, num_pages;
+  float scale_log2;            // softmax scale * k_scale * log2(e)
 };
 
 __device__ __forceinline__ float to_float(__half x) { return __half2float(x); }
 __device__ __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
 
+// ---- warp-level tensor-core helpers (mma.sync m16n8k16, f32 accumulate).
+// The decode streams every key once and has at most 8 query heads per tile,
+// so its products are tiny; warp-level MMAs from registers are enough to keep
+// it HBM-bound, where CUDA-core FMAs were not (fp8 halves the bytes per key).
 template <bool BF16>
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if (BF16) {
-      __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-      float2 t = __bfloat1622float2(h);
-      f[2 * i] = t.x;
-      f[2 * i + 1] = t.y;
-    } else {
-      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-      float2 t = __half22float2(h);
-      f[2 * i] = t.x;
-      f[2 * i + 1] = t.y;
-    }
-  }
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  if (BF16)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int D, int G, bool BF16>
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
+  if (BF16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Two e4m3 values in the low 16 bits (first value in the low byte) -> f16x2.
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two & 0xffffu), __NV_E4M3);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 4-byte global -> shared copy that bypasses registers; src_bytes 0 writes zeros
+// and reads nothing.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+template <int D, int G, bool QBF16, int KV>
 __global__ void __launch_bounds__(kThreadsDec, 1)
     decode_partial_kernel(const __grid_constant__ CUtensorMap tk,
                           const __grid_constant__ CUtensorMap tv, const DecArgs a) {
-  using C = DecCfg<D>;
-  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  constexpr int DL = D / 32;  // value columns per lane
+  using C = DecCfg<D, KV>;
+  using T = typename std::conditional<QBF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -106,8 +199,16 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   const int64_t pair = blockIdx.x / a.nsplit;  // b * Hkv + kh
   const int64_t b = pair / a.Hkv;
   const int kh = static_cast<int>(pair % a.Hkv);
+  int64_t len = a.S;
+  if (a.seq_lens) {
+    len = a.seq_lens[b];
+    if (len < 0 || len > a.S) {
+      if (threadIdx.x == 0 && split == 0) atomicExch(a.status, kStatusBadSeqLen);
+      len = len < 0 ? 0 : a.S;
+    }
+  }
   const int64_t k0 = static_cast<int64_t>(split) * a.chunk;
-  const int64_t k1 = (k0 + a.chunk < a.S) ? k0 + a.chunk : a.S;
+  const int64_t k1 = (k0 + a.chunk < len) ? k0 + a.chunk : len;
   const int ntiles = k1 > k0 ? static_cast<int>((k1 - k0 + kTileKeys - 1) / kTileKeys) : 0;
 
   if (threadIdx.x == 0) {
@@ -125,26 +226,76 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
 
   if (warp == kWarpsC) {
     // ------------------------------------------------------------ producer
+    // One lane waits and issues; the rest of the warp parks at the CTA
+    // barrier. (Polling the stage barriers from all 32 lanes, converged or
+    // not, slows the whole CTA by ~40 %.)
     if (lane == 0) {
-      int last[C::kStages];
-#pragma unroll
-      for (int s = 0; s < C::kStages; ++s) last[s] = -1;
+      const int n_pc = kTileKeys / a.piece_rows;  // 1, 2 or 4 pieces per tile
+      // Block-table windows of 32 logical pages, double-buffered in shared
+      // memory and filled by cp.async one window ahead, so reading a page
+      // number never waits on global memory.
+      int32_t* bt_s = reinterpret_cast<int32_t*>(smem + C::kBtOff);
+      const int32_t* bt_row = a.block_table ? a.block_table + b * a.max_pages : nullptr;
+      auto bt_fill = [&](int w) {  // logical pages [w, w + 32) -> buffer (w / 32) % 2
+        int32_t* dst = bt_s + ((w >> 5) & 1) * 32;
+        for (int i = 0; i < 32; ++i) {
+          const int64_t idx = static_cast<int64_t>(w) + i;
+          const bool in = idx < a.max_pages;
+          cp_async4(dst + i, bt_row + (in ? idx : 0), in ? 4 : 0);
+        }
+        cp_async_commit();
+      };
+      int win = -1;
+      if (a.block_table && ntiles > 0) {
+        win = static_cast<int>(k0 / a.page_size) & ~31;
+        bt_fill(win);
+        bt_fill(win + 32);
+        cp_async_wait_group1();  // the first window has landed
+      }
+      int issued = 0;
       for (int t = 0; t < ntiles; ++t) {
         const int st = t % C::kStages;
         if (!mbar_wait(empty + st, ((t / C::kStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
         mbar_expect_tx(full + st, C::kStageBytes);
         uint8_t* base = smem + st * C::kStageBytes;
-        const int32_t row = static_cast<int32_t>(k0 + static_cast<int64_t>(t) * kTileKeys);
-        for (int bx = 0; bx < C::kBoxes; ++bx) {
-          tma_load_3d(base + bx * (kTileKeys * 128), &tk, full + st, bx * 64, row, static_cast<int32_t>(pair));
-          tma_load_3d(base + C::kTileBytes + bx * (kTileKeys * 128), &tv, full + st, bx * 64, row,
-                      static_cast<int32_t>(pair));
-        }
-        last[st] = t;
-      }
+        const int32_t key0 = static_cast<int32_t>(k0 + static_cast<int64_t>(t) * kTileKeys);
 #pragma unroll
-      for (int s = 0; s < C::kStages; ++s)
-        if (last[s] >= 0) mbar_drain(full + s, (last[s] / C::kStages) & 1);
+        for (int p = 0; p < 4; ++p) {
+          if (p >= n_pc) break;
+          const int32_t key = key0 + p * a.piece_rows;
+          int32_t page = static_cast<int32_t>(b), row = key;
+          if (a.block_table) {
+            const int32_t lp = key / a.page_size;  // logical page of this piece
+            row = key - lp * a.page_size;
+            const int w = lp & ~31;
+            if (w != win) {  // the next window (pieces advance by at most one page)
+              win = w;
+              bt_fill(w + 32);         // refill the buffer of the window just left
+              cp_async_wait_group1();  // window w (issued one window ago) has landed
+            }
+            page = bt_s[((w >> 5) & 1) * 32 + (lp - w)];
+            if (key >= len) {
+              page = -1;  // past the sequence end: the box reads as zeros
+            } else if (page < 0 || page >= a.num_pages) {
+              atomicExch(a.status, kStatusBadPage);
+              page = -1;
+            }
+          }
+          uint8_t* dst = base + p * a.piece_rows * C::kBoxBytes;
+          for (int bx = 0; bx < C::kBoxes; ++bx) {
+            tma_load_4d(dst + bx * (kTileKeys * C::kBoxBytes), &tk, full + st, bx * C::kBoxCols, row, kh, page);
+            tma_load_4d(dst + C::kTileBytes + bx * (kTileKeys * C::kBoxBytes), &tv, full + st, bx * C::kBoxCols,
+                        row, kh, page);
+          }
+        }
+        issued = t + 1;
+      }
+      cp_async_wait_all();  // no copy into shared memory outlives the CTA
+      const int n = issued < C::kStages ? issued : C::kStages;
+      for (int s = 0; s < n; ++s) {
+        const int last = s + ((issued - 1 - s) / C::kStages) * C::kStages;
+        mbar_drain(full + s, (last / C::kStages) & 1);
+      }
     }
     __syncwarp();
     __syncthreads();
@@ -152,14 +303,59 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   }
 
   // -------------------------------------------------------------- compute
-  float m_run[G], l_run[G], acc[G][DL];
+  // Per 32-key tile, on tensor cores (m16n8k16, fp32 accumulators):
+  //   S   = Q K^T    M = 16 query rows (the G heads, zero-padded), N = 8 keys
+  //                  per n-tile (4 n-tiles), K = head dim;
+  //   O^T = V^T P^T  M = 16 value columns per m-tile (D/16 m-tiles), N = 8
+  //                  heads, K = 16 keys per step (2 steps).
+  // The S accumulator of a thread (head g = lane/4, keys 2c, 2c+1 of each
+  // n-tile, c = lane%4) is exactly its B fragment of P^T, so P never leaves
+  // registers. Softmax runs on the S accumulators; each thread's per-head
+  // running max/sum covers head g, and the O^T columns it owns (heads 2c,
+  // 2c+1) fetch their rescale factors by two shuffles.
+  // Operands: fp16/bf16 tiles by ldmatrix (K) / ldmatrix.trans (V); fp8 tiles
+  // by 16-byte loads converted in registers (e4m3x2 -> f16x2). For fp8 the
+  // head-dim elements are assigned to threads in a permuted order (thread c
+  // owns a contiguous quarter of each key row for Q K^T, and thread g owns a
+  // contiguous eighth of each value row for P V): a dot product does not
+  // depend on the order of its terms, and the output columns are written
+  // back to their true positions.
+  // MMA type: bf16 for bf16 caches, otherwise f16 (fp8 values are exact in
+  // f16; a bf16 query is scaled by a power of two into f16 range first).
+  constexpr bool kMmaBf16 = KV == kKvBF16;
+  constexpr bool kF8 = KV == kKvE4M3;
+  constexpr int KS = D / 16;   // k-steps of Q K^T
+  constexpr int MT = D / 16;   // m-tiles of P V
+  const int g = lane >> 2, c = lane & 3;
+  float sl2 = a.scale_log2;
+  float qs = 1.f;
+  if (QBF16 && kF8) {
+    float mx = 0.f;
+    for (int i = lane; i < G * D; i += 32) mx = fmaxf(mx, fabsf(sq[i]));
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m_run[h] = -INFINITY;
-    l_run[h] = 0.f;
-#pragma unroll
-    for (int c = 0; c < DL; ++c) acc[h][c] = 0.f;
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (mx > 0.f && mx <= 3.0e38f) {
+      int e = ((__float_as_int(mx) >> 23) & 0xff) - 127;  // floor(log2(max |q|)) for normal values
+      e = e < -100 ? -100 : e;
+      qs = __int_as_float((127 + 14 - e) << 23);         // max |q| * qs in [2^14, 2^15)
+      sl2 = a.scale_log2 * __int_as_float((127 - 14 + e) << 23);
+    }
   }
+  uint32_t qa[KS][2];  // A fragments of Q: rows g (a0, a2); rows g + 8 are zero
+#pragma unroll
+  for (int s = 0; s < KS; ++s) {
+    const int d0 = kF8 ? (D / 4) * c + 4 * s : 16 * s + 2 * c;
+    const int d1 = kF8 ? d0 + 2 : d0 + 8;
+    const float* qr = sq + (g < G ? g : 0) * D;
+    const float z = g < G ? qs : 0.f;
+    qa[s][0] = pack_pair<kMmaBf16>(qr[d0] * z, qr[d0 + 1] * z);
+    qa[s][1] = pack_pair<kMmaBf16>(qr[d1] * z, qr[d1 + 1] * z);
+  }
+  float o[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+
   for (int t = warp; t < ntiles; t += kWarpsC) {
     const int st = t % C::kStages;
     bool ok = mbar_wait(full + st, (t / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag);
@@ -167,111 +363,147 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
     if (!ok) break;
     const uint8_t* kt = smem + st * C::kStageBytes;
     const uint8_t* vt = kt + C::kTileBytes;
-    // scores: lane <-> key
-    float s[G];
+    const int64_t tile0 = k0 + static_cast<int64_t>(t) * kTileKeys;
+    const int rem = static_cast<int>(k1 - tile0 < kTileKeys ? k1 - tile0 : kTileKeys);
+
+    // ---- S = Q K^T
+    float sacc[4][4];
 #pragma unroll
-    for (int h = 0; h < G; ++h) s[h] = 0.f;
+    for (int nt = 0; nt < 4; ++nt) {
+      sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+      if (kF8) {
+        uint32_t kw[D / 16];
+        const int row = 8 * nt + g;
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      const int bx = c / 8, ch = c % 8;
-      const uint4 u = *reinterpret_cast<const uint4*>(kt + bx * (kTileKeys * 128) + lane * 128 +
-                                                      ((ch ^ (lane & 7)) * 16));
-      float kf[8];
-      unpack8<BF16>(u, kf);
+        for (int i = 0; i < D / 64; ++i) {
+          const uint4 u = *reinterpret_cast<const uint4*>(kt + C::off(row, (D / 4) * c + 16 * i));
+          kw[4 * i] = u.x;
+          kw[4 * i + 1] = u.y;
+          kw[4 * i + 2] = u.z;
+          kw[4 * i + 3] = u.w;
+        }
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float4 q0 = *reinterpret_cast<const float4*>(sq + h * D + c * 8);
-        const float4 q1 = *reinterpret_cast<const float4*>(sq + h * D + c * 8 + 4);
-        s[h] = fmaf(q0.x, kf[0], s[h]);
-        s[h] = fmaf(q0.y, kf[1], s[h]);
-        s[h] = fmaf(q0.z, kf[2], s[h]);
-        s[h] = fmaf(q0.w, kf[3], s[h]);
-        s[h] = fmaf(q1.x, kf[4], s[h]);
-        s[h] = fmaf(q1.y, kf[5], s[h]);
-        s[h] = fmaf(q1.z, kf[6], s[h]);
-        s[h] = fmaf(q1.w, kf[7], s[h]);
-      }
-    }
-    const int64_t key = k0 + static_cast<int64_t>(t) * kTileKeys + lane;
-    float p[G];
+        for (int s = 0; s < KS; ++s)
+          mma16816<kMmaBf16>(sacc[nt], qa[s][0], 0u, qa[s][1], 0u, e4m3x2_to_h2(kw[s]), e4m3x2_to_h2(kw[s] >> 16));
+      } else {
+        const int row = 8 * nt + (lane & 7);
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      float x = key < k1 ? s[h] * a.scale_log2 : -INFINITY;
-      float mx = x;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_new = fmaxf(m_run[h], mx);  // finite: the tile has >= 1 valid key
-      const float alpha = ex2(m_run[h] - m_new);
-      p[h] = ex2(x - m_new);
-      l_run[h] = l_run[h] * alpha + p[h];  // lane-local partial sum
-      m_run[h] = m_new;
-#pragma unroll
-      for (int c = 0; c < DL; ++c) acc[h][c] *= alpha;
-    }
-    // P V: lane <-> value columns
-#pragma unroll 4
-    for (int j = 0; j < kTileKeys; ++j) {
-      float vf[DL];
-      {
-        // columns [lane*DL, lane*DL + DL) of row j; 64-column boxes, swizzled 16-byte chunks
-        const int col = lane * DL;
-        const int bx = col / 64, cb = (col % 64) * 2;  // byte offset inside the 128-byte row
-        const uint8_t* rowp = vt + bx * (kTileKeys * 128) + j * 128;
-        const int chunk = (cb >> 4) ^ (j & 7);
-        const uint8_t* src = rowp + chunk * 16 + (cb & 15);
-        if (DL == 4) {
-          const uint2 u = *reinterpret_cast<const uint2*>(src);
-          float2 a0, a1;
-          if (BF16) {
-            a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-            a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-          } else {
-            a0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-            a1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-          }
-          vf[0] = a0.x;
-          vf[1] = a0.y;
-          vf[DL > 2 ? 2 : 0] = a1.x;
-          vf[DL > 3 ? 3 : 1] = a1.y;
-        } else {
-          const uint32_t u = *reinterpret_cast<const uint32_t*>(src);
-          float2 a0 = BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u))
-                           : __half22float2(*reinterpret_cast<const __half2*>(&u));
-          vf[0] = a0.x;
-          vf[DL > 1 ? 1 : 0] = a0.y;
+        for (int s2 = 0; s2 < KS / 2; ++s2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kt + C::off(row, (4 * s2 + (lane >> 3)) * 16), b0, b1, b2, b3);
+          mma16816<kMmaBf16>(sacc[nt], qa[2 * s2][0], 0u, qa[2 * s2][1], 0u, b0, b1);
+          mma16816<kMmaBf16>(sacc[nt], qa[2 * s2 + 1][0], 0u, qa[2 * s2 + 1][1], 0u, b2, b3);
         }
       }
+    }
+
+    // ---- online softmax (head g; keys 8 nt + 2c + j)
+    float mx = -INFINITY;
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float pj = __shfl_sync(0xffffffffu, p[h], j);
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-        for (int c = 0; c < DL; ++c) acc[h][c] = fmaf(pj, vf[c], acc[h][c]);
+      for (int j = 0; j < 2; ++j) {
+        const float x = (8 * nt + 2 * c + j) < rem ? sacc[nt][j] * sl2 : -INFINITY;
+        sacc[nt][j] = x;
+        mx = fmaxf(mx, x);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);  // finite: the tile has >= 1 valid key
+    const float alpha = ex2(m_run - m_new);
+    m_run = m_new;
+    float psum = 0.f;
+    uint32_t pb[2][2];  // B fragments of P^T for the two 16-key steps
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const float p0 = ex2(sacc[nt][0] - m_new), p1 = ex2(sacc[nt][1] - m_new);
+      psum += p0 + p1;
+      pb[nt >> 1][nt & 1] = pack_pair<kMmaBf16>(p0, p1);
+    }
+    l_run = l_run * alpha + psum;
+    const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * c);      // head 2c
+    const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);  // head 2c + 1
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      o[mt][0] *= al0;
+      o[mt][1] *= al1;
+      o[mt][2] *= al0;
+      o[mt][3] *= al1;
+    }
+
+    // ---- O^T += V^T P^T
+#pragma unroll
+    for (int sp = 0; sp < 2; ++sp) {
+      const int kb = 16 * sp;
+      if (kF8) {
+        constexpr int W = D / 32;  // 32-bit words of a thread's eighth of a value row
+        uint32_t r[4][W];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = kb + 2 * c + (i & 1) + 8 * (i >> 1);
+          const uint8_t* src = vt + C::off(row, (D / 8) * g);
+          if (W == 4) {
+            const uint4 u = *reinterpret_cast<const uint4*>(src);
+            r[i][0] = u.x;
+            r[i][W > 1 ? 1 : 0] = u.y;
+            r[i][W > 2 ? 2 : 0] = u.z;
+            r[i][W > 3 ? 3 : 0] = u.w;
+          } else {
+            const uint2 u = *reinterpret_cast<const uint2*>(src);
+            r[i][0] = u.x;
+            r[i][W > 1 ? 1 : 0] = u.y;
+          }
+          if (row >= rem)
+#pragma unroll
+            for (int w = 0; w < W; ++w) r[i][w] = 0u;  // rows past the end may hold anything
+        }
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          const uint32_t x01 = byte_perm(r[0][w], r[1][w], 0x5140), y01 = byte_perm(r[0][w], r[1][w], 0x7362);
+          const uint32_t x23 = byte_perm(r[2][w], r[3][w], 0x5140), y23 = byte_perm(r[2][w], r[3][w], 0x7362);
+          mma16816<kMmaBf16>(o[2 * w], e4m3x2_to_h2(x01), e4m3x2_to_h2(x01 >> 16), e4m3x2_to_h2(x23),
+                             e4m3x2_to_h2(x23 >> 16), pb[sp][0], pb[sp][1]);
+          mma16816<kMmaBf16>(o[2 * w + 1], e4m3x2_to_h2(y01), e4m3x2_to_h2(y01 >> 16), e4m3x2_to_h2(y23),
+                             e4m3x2_to_h2(y23 >> 16), pb[sp][0], pb[sp][1]);
+        }
+      } else {
+        const int m = lane >> 3;
+        const int row = kb + 8 * (m >> 1) + (lane & 7);
+        // keys of this thread's A fragment halves: a0/a1 -> kb + 2c (+1), a2/a3 -> kb + 8 + 2c (+1)
+        const uint32_t mlo = (kb + 2 * c < rem ? 0x0000ffffu : 0u) | (kb + 2 * c + 1 < rem ? 0xffff0000u : 0u);
+        const uint32_t mhi = (kb + 8 + 2 * c < rem ? 0x0000ffffu : 0u) | (kb + 9 + 2 * c < rem ? 0xffff0000u : 0u);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(vt + C::off(row, (2 * mt + (m & 1)) * 16), a0, a1, a2, a3);
+          mma16816<kMmaBf16>(o[mt], a0 & mlo, a1 & mlo, a2 & mhi, a3 & mhi, pb[sp][0], pb[sp][1]);
+        }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + st);
   }
 
-  // Lane-local sums -> warp sums.
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int o = 16; o; o >>= 1) l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], o);
+  // Per-thread sums -> per-head sums (the four threads of head g).
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
   __syncthreads();  // every tile consumed and landed: the ring is free for the merge
   float* mw = reinterpret_cast<float*>(smem);                 // [8][G] m
   float* lw = mw + kWarpsC * G;                              // [8][G] l
   float* aw = lw + kWarpsC * G;                              // [8][G][D] acc
-  if (lane == 0)
+  if (c == 0 && g < G) {
+    mw[warp * G + g] = m_run;
+    lw[warp * G + g] = l_run;
+  }
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      mw[warp * G + h] = m_run[h];
-      lw[warp * G + h] = l_run[h];
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int h = 2 * c + (i & 1), half = i >> 1;
+      const int d = kF8 ? (D / 8) * g + 2 * mt + half : 16 * mt + 8 * half + g;
+      if (h < G) aw[(warp * G + h) * D + d] = o[mt][i];
     }
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int c = 0; c < DL; ++c) aw[(warp * G + h) * D + lane * DL + c] = acc[h][c];
   asm volatile("bar.sync 1, %0;" ::"n"(kWarpsC * 32));
   for (int i = threadIdx.x; i < G * D; i += kWarpsC * 32) {
     const int h = i / D, d = i % D;
@@ -296,9 +528,10 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   }
 }
 
-template <int D, bool BF16>
+template <int D, bool QBF16>
 __global__ void __launch_bounds__(D) decode_combine_kernel(const float* ws_acc, const float* ws_ml,
-                                                           void* out, float* lse, int nsplit) {
+                                                           void* out, float* lse, int nsplit,
+                                                           float v_scale) {
   const int64_t qh = blockIdx.x;
   const int d = threadIdx.x;
   float M = -INFINITY;
@@ -310,42 +543,39 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* ws_acc, 
     o = fmaf(f, ws_acc[(qh * nsplit + s) * D + d], o);
     l = fmaf(f, ws_ml[(qh * nsplit + s) * 2 + 1], l);
   }
-  const float r = l > 0.f ? o / l : 0.f;
-  if (BF16)
+  const float r = l > 0.f ? (o / l) * v_scale : 0.f;
+  if (QBF16)
     static_cast<__nv_bfloat16*>(out)[qh * D + d] = __float2bfloat16_rn(r);
   else
     static_cast<__half*>(out)[qh * D + d] = __float2half_rn(r);
   if (lse && d == 0) lse[qh] = l > 0.f ? (M + __log2f(l)) * kLn2f : -INFINITY;
 }
 
+// A decode problem in cache terms. The dense operands of pa_decode_fwd map to
+// one page per sequence (page_size = S, pages = B) and no block table.
 struct DecPlan {
   int64_t B, Hq, Hkv, S;
   int D, G, nsplit, chunk;
-  bool bf16;
+  bool q_bf16;
+  int kv;                       // kKvF16 / kKvBF16 / kKvE4M3
+  int64_t page_size, num_pages, max_pages;
+  int64_t key_stride, head_stride, page_stride;  // elements
+  bool paged;
+  int piece_rows;
+  double scale;
+  float k_scale, v_scale;
 };
 
-pa_status make_plan(const pa_sdpa_desc& d, DecPlan* p) {
-  if (d.L != 1) return fail(PA_ERR_UNSUPPORTED, "decode: query length must be 1");
-  if (d.dtype != PA_F16 && d.dtype != PA_BF16) return fail(PA_ERR_UNSUPPORTED, "decode: dtype must be fp16/bf16");
-  if (d.E != d.Ev || (d.E != 64 && d.E != 128)) return fail(PA_ERR_UNSUPPORTED, "decode: head dim must be 64 or 128");
-  if (d.mask_kind != PA_MASK_NONE || d.is_causal) return fail(PA_ERR_UNSUPPORTED, "decode: no mask / causal");
-  if (d.S < 1) return fail(PA_ERR_UNSUPPORTED, "decode: needs at least one key");
-  int64_t n, H, Hkv;
-  if (!dense_bhsd(d, &n, &H, &Hkv)) return fail(PA_ERR_UNSUPPORTED, "decode: operands not dense (B, H, S, D)");
-  const int64_t G = H / Hkv;
-  if (G != 1 && G != 2 && G != 4 && G != 8) return fail(PA_ERR_UNSUPPORTED, "decode: group size must be 1, 2, 4 or 8");
-  if (d.S > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "decode: too many keys");
-  p->B = n / H;
-  p->Hq = H;
-  p->Hkv = Hkv;
-  p->S = d.S;
-  p->D = static_cast<int>(d.E);
-  p->G = static_cast<int>(G);
-  p->bf16 = d.dtype == PA_BF16;
-  // Split the keys so that the CTA count fills whole waves (1 CTA per SM).
-  const int64_t pairs = p->B * Hkv;
+// Splits the keys so that the CTA count fills whole waves (1 CTA per SM).
+void split_keys(DecPlan* p) {
+  const int64_t pairs = p->B * p->Hkv;
   const int64_t sms = sm_count();
-  const int64_t tiles = (d.S + kTileKeys - 1) / kTileKeys;
+  const int64_t tiles = (p->S + kTileKeys - 1) / kTileKeys;
+  if (tiles == 0) {
+    p->nsplit = 1;
+    p->chunk = kTileKeys;
+    return;
+  }
   int best = 1;
   double best_eff = 0;
   for (int ns = 1; ns <= 64 && ns <= tiles; ++ns) {
@@ -360,10 +590,97 @@ pa_status make_plan(const pa_sdpa_desc& d, DecPlan* p) {
       best = ns;
     }
   }
-  p->nsplit = best;
   const int64_t per = (tiles + best - 1) / best;
   p->chunk = static_cast<int>(per * kTileKeys);
-  p->nsplit = static_cast<int>((d.S + p->chunk - 1) / p->chunk);
+  p->nsplit = static_cast<int>((p->S + p->chunk - 1) / p->chunk);
+}
+
+pa_status check_shape(DecPlan* p) {
+  if (p->D != 64 && p->D != 128) return fail(PA_ERR_UNSUPPORTED, "decode: head dim must be 64 or 128");
+  if (p->Hkv < 1 || p->Hq < 1 || p->Hq % p->Hkv) return fail(PA_ERR_INVALID, "decode: q heads must be a multiple of kv heads");
+  const int64_t G = p->Hq / p->Hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return fail(PA_ERR_UNSUPPORTED, "decode: group size must be 1, 2, 4 or 8");
+  p->G = static_cast<int>(G);
+  if (p->S < 0 || p->S > 0x7fffffffLL - kTileKeys) return fail(PA_ERR_UNSUPPORTED, "decode: too many keys");
+  return PA_OK;
+}
+
+pa_status make_plan(const pa_sdpa_desc& d, DecPlan* p) {
+  if (d.L != 1) return fail(PA_ERR_UNSUPPORTED, "decode: query length must be 1");
+  if (d.dtype != PA_F16 && d.dtype != PA_BF16) return fail(PA_ERR_UNSUPPORTED, "decode: dtype must be fp16/bf16");
+  if (d.E != d.Ev || (d.E != 64 && d.E != 128)) return fail(PA_ERR_UNSUPPORTED, "decode: head dim must be 64 or 128");
+  if (d.mask_kind != PA_MASK_NONE || d.is_causal) return fail(PA_ERR_UNSUPPORTED, "decode: no mask / causal");
+  if (d.S < 1) return fail(PA_ERR_UNSUPPORTED, "decode: needs at least one key");
+  int64_t n, H, Hkv;
+  if (!dense_bhsd(d, &n, &H, &Hkv)) return fail(PA_ERR_UNSUPPORTED, "decode: operands not dense (B, H, S, D)");
+  *p = DecPlan{};
+  p->B = n / H;
+  p->Hq = H;
+  p->Hkv = Hkv;
+  p->S = d.S;
+  p->D = static_cast<int>(d.E);
+  PA_TRY(check_shape(p));
+  p->q_bf16 = d.dtype == PA_BF16;
+  p->kv = p->q_bf16 ? kKvBF16 : kKvF16;
+  p->page_size = d.S;
+  p->num_pages = p->B;
+  p->max_pages = 1;
+  p->key_stride = p->D;
+  p->head_stride = d.S * p->D;
+  p->page_stride = Hkv * d.S * p->D;
+  p->paged = false;
+  p->piece_rows = kTileKeys;
+  p->scale = d.scale;
+  p->k_scale = 1.f;
+  p->v_scale = 1.f;
+  split_keys(p);
+  return PA_OK;
+}
+
+pa_status make_plan(const pa_kv_cache_desc& d, bool paged, DecPlan* p) {
+  *p = DecPlan{};
+  if (d.q_dtype != PA_F16 && d.q_dtype != PA_BF16) return fail(PA_ERR_UNSUPPORTED, "decode: q dtype must be fp16 or bf16");
+  if (d.kv_dtype != d.q_dtype && d.kv_dtype != PA_FP8_E4M3)
+    return fail(PA_ERR_UNSUPPORTED, "decode: the cache dtype must be the query's dtype or fp8 e4m3");
+  if (d.batch < 0) return fail(PA_ERR_INVALID, "decode: negative batch");
+  if (!std::isfinite(d.scale) || !std::isfinite(d.k_scale) || !std::isfinite(d.v_scale))
+    return fail(PA_ERR_INVALID, "decode: scale, k_scale and v_scale must be finite");
+  p->B = d.batch;
+  p->Hq = d.q_heads;
+  p->Hkv = d.kv_heads;
+  p->S = d.max_seq_len;
+  p->D = static_cast<int>(d.head_dim);
+  if (d.head_dim != p->D) return fail(PA_ERR_UNSUPPORTED, "decode: head dim must be 64 or 128");
+  PA_TRY(check_shape(p));
+  p->q_bf16 = d.q_dtype == PA_BF16;
+  p->kv = d.kv_dtype == PA_FP8_E4M3 ? kKvE4M3 : (p->q_bf16 ? kKvBF16 : kKvF16);
+  p->page_size = d.page_size;
+  p->num_pages = d.num_pages;
+  p->max_pages = d.max_pages_per_seq;
+  p->key_stride = d.key_stride;
+  p->head_stride = d.head_stride;
+  p->page_stride = d.page_stride;
+  p->paged = paged;
+  p->scale = d.scale;
+  p->k_scale = d.k_scale;
+  p->v_scale = d.v_scale;
+  if (d.key_stride < p->D || d.head_stride < 1 || d.page_stride < 1)
+    return fail(PA_ERR_INVALID, "decode: cache strides must be positive and key_stride >= head_dim");
+  if (d.num_pages < 1 || d.num_pages > 0x7fffffffLL) return fail(PA_ERR_INVALID, "decode: num_pages must be in [1, 2^31)");
+  if (paged) {
+    if (d.page_size < 8 || d.page_size % 8) return fail(PA_ERR_UNSUPPORTED, "decode: page_size must be a positive multiple of 8");
+    if (d.page_size > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "decode: page_size too large");
+    if (d.max_pages_per_seq < (d.max_seq_len + d.page_size - 1) / d.page_size)
+      return fail(PA_ERR_INVALID, "decode: max_pages_per_seq * page_size must cover max_seq_len");
+    p->piece_rows = d.page_size % 32 == 0 ? 32 : (d.page_size % 16 == 0 ? 16 : 8);
+  } else {
+    if (d.num_pages < d.batch) return fail(PA_ERR_INVALID, "decode: without a block table the cache needs one page per sequence");
+    if (d.page_size < d.max_seq_len || d.page_size < 1 || d.page_size > 0x7fffffffLL)
+      return fail(PA_ERR_INVALID, "decode: without a block table page_size must be at least max_seq_len");
+    p->max_pages = 1;
+    p->piece_rows = kTileKeys;
+  }
+  split_keys(p);
   return PA_OK;
 }
 
@@ -372,31 +689,87 @@ size_t plan_ws_bytes(const DecPlan& p) {
   return slots * (p.D + 2) * sizeof(float);
 }
 
-template <int D, int G, bool BF16>
+template <int D, int G, bool QBF16, int KV>
 pa_status launch_dec(const DecPlan& p, const CUtensorMap& tk, const CUtensorMap& tv, DecArgs& a,
                      void* out, float* lse, cudaStream_t st) {
-  auto kern = decode_partial_kernel<D, G, BF16>;
-  constexpr int smem = DecCfg<D>::kSmemBytes;
+  auto kern = decode_partial_kernel<D, G, QBF16, KV>;
+  constexpr int smem = DecCfg<D, KV>::kSmemBytes;
   static uint64_t attr_set = 0;
   PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, &attr_set));
   const int64_t grid = p.B * p.Hkv * p.nsplit;
   kern<<<static_cast<unsigned>(grid), kThreadsDec, smem, st>>>(tk, tv, a);
   PA_CUDA(cudaGetLastError());
-  decode_combine_kernel<D, BF16><<<static_cast<unsigned>(p.B * p.Hq), D, 0, st>>>(
-      a.ws_acc, a.ws_ml, out, lse, p.nsplit);
+  decode_combine_kernel<D, QBF16><<<static_cast<unsigned>(p.B * p.Hq), D, 0, st>>>(
+      a.ws_acc, a.ws_ml, out, lse, p.nsplit, p.v_scale);
   PA_CUDA(cudaGetLastError());
   return PA_OK;
 }
 
-template <int D, bool BF16>
+template <int D, bool QBF16, int KV>
 pa_status launch_dec_g(const DecPlan& p, const CUtensorMap& tk, const CUtensorMap& tv, DecArgs& a,
                        void* out, float* lse, cudaStream_t st) {
   switch (p.G) {
-    case 1: return launch_dec<D, 1, BF16>(p, tk, tv, a, out, lse, st);
-    case 2: return launch_dec<D, 2, BF16>(p, tk, tv, a, out, lse, st);
-    case 4: return launch_dec<D, 4, BF16>(p, tk, tv, a, out, lse, st);
-    default: return launch_dec<D, 8, BF16>(p, tk, tv, a, out, lse, st);
+    case 1: return launch_dec<D, 1, QBF16, KV>(p, tk, tv, a, out, lse, st);
+    case 2: return launch_dec<D, 2, QBF16, KV>(p, tk, tv, a, out, lse, st);
+    case 4: return launch_dec<D, 4, QBF16, KV>(p, tk, tv, a, out, lse, st);
+    default: return launch_dec<D, 8, QBF16, KV>(p, tk, tv, a, out, lse, st);
   }
+}
+
+template <int D>
+pa_status launch_dec_t(const DecPlan& p, const CUtensorMap& tk, const CUtensorMap& tv, DecArgs& a,
+                       void* out, float* lse, cudaStream_t st) {
+  if (p.kv == kKvE4M3)
+    return p.q_bf16 ? launch_dec_g<D, true, kKvE4M3>(p, tk, tv, a, out, lse, st)
+                    : launch_dec_g<D, false, kKvE4M3>(p, tk, tv, a, out, lse, st);
+  return p.q_bf16 ? launch_dec_g<D, true, kKvBF16>(p, tk, tv, a, out, lse, st)
+                  : launch_dec_g<D, false, kKvF16>(p, tk, tv, a, out, lse, st);
+}
+
+pa_status encode_cache_map(const DecPlan& p, const void* base, CUtensorMap* map) {
+  const int esz = p.kv == kKvE4M3 ? 1 : 2;
+  const int row_bytes = p.D * esz;
+  const uint32_t box_bytes = row_bytes < 128 ? row_bytes : 128;
+  const CUtensorMapDataType dt = p.kv == kKvE4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : p.kv == kKvBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t dims[4] = {static_cast<uint64_t>(p.D), static_cast<uint64_t>(p.page_size),
+                            static_cast<uint64_t>(p.Hkv), static_cast<uint64_t>(p.num_pages)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(p.key_stride) * esz,
+                               static_cast<uint64_t>(p.head_stride) * esz,
+                               static_cast<uint64_t>(p.page_stride) * esz};
+  return encode_tma_4d(map, dt, base, dims, strides, box_bytes / esz, static_cast<uint32_t>(p.piece_rows),
+                       box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+pa_status run_plan(const DecPlan& p, const void* q, const void* k, const void* v,
+                   const int32_t* block_table, const int32_t* seq_lens, void* out, float* lse,
+                   void* ws, size_t ws_bytes, int* status, cudaStream_t st) {
+  if (ws_bytes < plan_ws_bytes(p)) return fail(PA_ERR_INVALID, "decode: workspace too small");
+  if (p.B * p.Hkv * p.nsplit > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "decode: grid too large");
+  CUtensorMap tk, tv;
+  PA_TRY(encode_cache_map(p, k, &tk));
+  PA_TRY(encode_cache_map(p, v, &tv));
+  DecArgs a{};
+  a.q = q;
+  const size_t slots = static_cast<size_t>(p.B * p.Hq) * p.nsplit;
+  a.ws_acc = static_cast<float*>(ws);
+  a.ws_ml = a.ws_acc + slots * p.D;
+  a.status = status;
+  a.block_table = p.paged ? block_table : nullptr;
+  a.seq_lens = seq_lens;
+  a.S = p.S;
+  a.max_pages = p.max_pages;
+  a.Hq = static_cast<int32_t>(p.Hq);
+  a.Hkv = static_cast<int32_t>(p.Hkv);
+  a.nsplit = p.nsplit;
+  a.chunk = p.chunk;
+  a.page_size = static_cast<int32_t>(p.page_size);
+  a.piece_rows = p.piece_rows;
+  a.num_pages = static_cast<int32_t>(p.num_pages);
+  a.scale_log2 = static_cast<float>(p.scale * static_cast<double>(p.k_scale) * 1.4426950408889634);
+  if (p.D == 128) return launch_dec_t<128>(p, tk, tv, a, out, lse, st);
+  return launch_dec_t<64>(p, tk, tv, a, out, lse, st);
 }
 
 }  // namespace
@@ -408,32 +781,7 @@ pa_status run_decode_status(const pa_sdpa_desc& d, const void* q, const void* k,
                             cudaStream_t st) {
   DecPlan p;
   PA_TRY(make_plan(d, &p));
-  if (ws_bytes < plan_ws_bytes(p)) return fail(PA_ERR_INVALID, "decode: workspace too small");
-  const bool bf16 = p.bf16;
-  const CUtensorMapDataType tdt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap tk, tv;
-  const uint64_t rowb = static_cast<uint64_t>(p.D) * 2;
-  const uint64_t planes = static_cast<uint64_t>(p.B * p.Hkv);
-  PA_TRY(encode_tma_3d(&tk, tdt, k, p.D, p.S, planes, rowb, rowb * p.S, 64, kTileKeys, CU_TENSOR_MAP_SWIZZLE_128B));
-  PA_TRY(encode_tma_3d(&tv, tdt, v, p.D, p.S, planes, rowb, rowb * p.S, 64, kTileKeys, CU_TENSOR_MAP_SWIZZLE_128B));
-  DecArgs a{};
-  a.q = q;
-  const size_t slots = static_cast<size_t>(p.B * p.Hq) * p.nsplit;
-  a.ws_acc = static_cast<float*>(ws);
-  a.ws_ml = a.ws_acc + slots * p.D;
-  a.status = status;
-  a.S = p.S;
-  a.Hq = static_cast<int32_t>(p.Hq);
-  a.Hkv = static_cast<int32_t>(p.Hkv);
-  a.nsplit = p.nsplit;
-  a.chunk = p.chunk;
-  a.scale_log2 = static_cast<float>(d.scale * 1.4426950408889634);
-  if (p.B * p.Hkv * p.nsplit > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "decode: grid too large");
-  if (p.D == 128)
-    return bf16 ? launch_dec_g<128, true>(p, tk, tv, a, out, lse, st)
-                : launch_dec_g<128, false>(p, tk, tv, a, out, lse, st);
-  return bf16 ? launch_dec_g<64, true>(p, tk, tv, a, out, lse, st)
-              : launch_dec_g<64, false>(p, tk, tv, a, out, lse, st);
+  return run_plan(p, q, k, v, nullptr, nullptr, out, lse, ws, ws_bytes, status, st);
 }
 
 pa_status run_decode(const pa_sdpa_desc& d, const void* q, const void* k, const void* v, void* out,
@@ -477,6 +825,42 @@ extern "C" pa_status pa_decode_fwd(const pa_sdpa_desc* desc, const void* q, cons
   void* ws = nullptr;
   PA_TRY(scratch_alloc(&ws, need, st));
   pa_status s = run_decode(d, q, k, v, out, lse, ws, need, st);
+  scratch_free(ws, st);
+  return s;
+}
+
+extern "C" pa_status pa_decode_kv_workspace_size(const pa_kv_cache_desc* desc, int32_t paged,
+                                                 size_t* bytes) {
+  clear_error();
+  if (!desc || !bytes) return fail(PA_ERR_INVALID, "null argument");
+  DecPlan p;
+  PA_TRY(make_plan(*desc, paged != 0, &p));
+  *bytes = plan_ws_bytes(p);
+  return PA_OK;
+}
+
+extern "C" pa_status pa_decode_kv_fwd(const pa_kv_cache_desc* desc, const void* q,
+                                      const void* k_cache, const void* v_cache,
+                                      const int32_t* block_table, const int32_t* seq_lens,
+                                      void* out, float* lse, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!desc) return fail(PA_ERR_INVALID, "null descriptor");
+  DecPlan p;
+  PA_TRY(make_plan(*desc, block_table != nullptr, &p));
+  if (p.B == 0) return PA_OK;
+  if (!q || !k_cache || !v_cache || !out) return fail(PA_ERR_INVALID, "decode: null q, cache or out pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* status = device_status_word();
+  if (!status) return fail(PA_ERR_CUDA, "device status word unavailable");
+  const size_t need = plan_ws_bytes(p);
+  if (workspace) {
+    if (workspace_bytes < need) return fail(PA_ERR_INVALID, "decode: workspace smaller than pa_decode_kv_workspace_size");
+    return run_plan(p, q, k_cache, v_cache, block_table, seq_lens, out, lse, workspace, workspace_bytes, status, st);
+  }
+  void* ws = nullptr;
+  PA_TRY(scratch_alloc(&ws, need, st));
+  pa_status s = run_plan(p, q, k_cache, v_cache, block_table, seq_lens, out, lse, ws, need, status, st);
   scratch_free(ws, st);
   return s;
 }

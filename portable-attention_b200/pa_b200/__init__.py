@@ -19,13 +19,15 @@ from __future__ import annotations
 from ._lib import LibraryError, PaError, library_path
 from .autograd import forward_with_lse, sdpa_backward
 from .backend import scaled_dot_product_attention, sdpa_device
+from .kvcache import decode_kv_cache, decode_kv_device, kv_cache_desc
 from .device import (DeviceBuffer, Event, Stream, current_device, device_count, pinned_empty,
                      set_device, sync_device_status)
 from .plan import compute_dtype, plan_call
 
 __all__ = [
     "DeviceBuffer", "Event", "LibraryError", "PaError", "Stream", "available", "compute_dtype",
-    "current_device", "device_count", "forward_with_lse", "library_path", "pinned_empty",
+    "current_device", "decode_kv_cache", "decode_kv_device", "device_count", "forward_with_lse",
+    "kv_cache_desc", "library_path", "pinned_empty",
     "plan_call", "register", "scaled_dot_product_attention", "sdpa_backward", "sdpa_device",
     "set_device", "sync_device_status",
 ]

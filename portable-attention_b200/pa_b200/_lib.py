@@ -13,13 +13,13 @@ import threading
 from pathlib import Path
 
 __all__ = [
-    "PA_BF16", "PA_BOOL", "PA_F16", "PA_F32", "PA_F64", "PA_MASK_ADD", "PA_MASK_BOOL",
-    "PA_MASK_NONE", "PA_MAX_LEAD", "LibraryError", "PaError", "SdpaDesc", "check", "lib",
-    "library_path",
+    "PA_BF16", "PA_BOOL", "PA_F16", "PA_F32", "PA_F64", "PA_FP8_E4M3", "PA_MASK_ADD",
+    "PA_MASK_BOOL", "PA_MASK_NONE", "PA_MAX_LEAD", "KvCacheDesc", "LibraryError", "PaError",
+    "SdpaDesc", "check", "lib", "library_path",
 ]
 
 PA_OK, PA_ERR_INVALID, PA_ERR_UNSUPPORTED, PA_ERR_CUDA, PA_ERR_TIMEOUT, PA_ERR_NCCL, PA_ERR_NOMEM = range(7)
-PA_F16, PA_BF16, PA_F32, PA_F64, PA_BOOL = 1, 2, 3, 4, 5
+PA_F16, PA_BF16, PA_F32, PA_F64, PA_BOOL, PA_FP8_E4M3 = 1, 2, 3, 4, 5, 6
 PA_MASK_NONE, PA_MASK_BOOL, PA_MASK_ADD = 0, 1, 2
 PA_MAX_LEAD = 6
 
@@ -75,6 +75,29 @@ class SdpaDesc(ctypes.Structure):
     ]
 
 
+class KvCacheDesc(ctypes.Structure):
+    """Mirror of ``pa_kv_cache_desc`` (include/pa_b200.h)."""
+
+    _fields_ = [
+        ("q_dtype", ctypes.c_int32),
+        ("kv_dtype", ctypes.c_int32),
+        ("batch", ctypes.c_int64),
+        ("q_heads", ctypes.c_int64),
+        ("kv_heads", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64),
+        ("max_seq_len", ctypes.c_int64),
+        ("page_size", ctypes.c_int64),
+        ("num_pages", ctypes.c_int64),
+        ("max_pages_per_seq", ctypes.c_int64),
+        ("key_stride", ctypes.c_int64),
+        ("head_stride", ctypes.c_int64),
+        ("page_stride", ctypes.c_int64),
+        ("scale", ctypes.c_double),
+        ("k_scale", ctypes.c_float),
+        ("v_scale", ctypes.c_float),
+    ]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _DESC = ctypes.POINTER(SdpaDesc)
@@ -108,6 +131,8 @@ SIGNATURES = {
     "pa_decode_workspace_size": [_DESC, ctypes.POINTER(ctypes.c_size_t)],
     "pa_decode_fwd": [_DESC, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "pa_decode_fwd_static": [_DESC, _P, _P, _P, _P, _P, _P, _P],
+    "pa_decode_kv_workspace_size": [ctypes.POINTER(KvCacheDesc), _I32, ctypes.POINTER(ctypes.c_size_t)],
+    "pa_decode_kv_fwd": [ctypes.POINTER(KvCacheDesc), _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "pa_sdpa_bwd": [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "pa_comm_unique_id": [ctypes.c_char_p],
     "pa_comm_init": [ctypes.POINTER(_P), ctypes.c_char_p, _I32, _I32],
