@@ -17,22 +17,21 @@
 // per-tensor dequantisation scales: k_scale folds into the softmax scale and
 // v_scale into the final normalisation.
 //
-// CTA = 1 producer warp + 8 compute warps.
-//   producer  TMA-loads 32-key K and V tiles (128-byte swizzle, or 64-byte for
-//             64-byte rows) into a ring of shared-memory stages (a multiple
-//             of 8 stages, so each stage always serves the same compute
-//             warp); keeps up to 192 KB in flight per SM so HBM stays busy. For a paged cache it
-//             stages the block table in shared memory 32 entries at a time,
-//             one window ahead (cp.async), and splits a tile into 16- or 8-row
-//             pieces when pages are shorter than 32 keys.
-//   compute   warp w consumes tiles w, w+8, w+16, ... on its own, on tensor
-//             cores (warp-level m16n8k16, fp32 accumulators): S = Q K^T for
-//             the G query heads (zero-padded to 16 rows), online softmax on
-//             the accumulators, O^T += V^T P^T with P straight from those
-//             accumulators. fp8 tiles are converted to f16 in registers.
-//             Keys past the sequence end are masked and their value rows
-//             zeroed, so stale cache contents (even NaN) never reach the
-//             output.
+// CTA = 8 warps. Warp w owns tiles w, w+8, w+16, ... of the CTA's key range
+// (a tile is 4 KB of keys + 4 KB of values: 16, 32 or 64 keys) and three
+// 8 KB shared-memory stages: it keeps three tiles in flight by TMA (128-byte
+// swizzle, or 64-byte for 64-byte rows; 192 KB per SM) and refills a stage as
+// soon as it has used it, so no warp waits on another. For a paged cache the
+// page numbers of the next tile to load are read from the block table one
+// tile ahead, one piece per lane; a tile is split into pieces of 8-32 rows
+// when pages are shorter than a tile.
+//   compute   on tensor cores (warp-level m16n8k16, fp32 accumulators):
+//             S = Q K^T for the G query heads (zero-padded to 16 rows),
+//             online softmax on the accumulators, O^T += V^T P^T with P
+//             straight from those accumulators. fp8 tiles are converted to
+//             f16 in registers. Keys past the sequence end are masked and
+//             their value rows zeroed, so stale cache contents (even NaN)
+//             never reach the output.
 //             The 8 warps' partial states merge in shared memory at the end
 //             and the CTA writes one partial (m, l, acc[D]) per query head
 //             into the workspace.
@@ -56,12 +55,17 @@
 namespace pa {
 namespace {
 
-constexpr int kWarpsC = 8;                 // compute warps
-constexpr int kThreadsDec = 32 * (kWarpsC + 1);
-constexpr int kTileKeys = 32;
+constexpr int kWarpsC = 8;                 // compute warps (each loads its own tiles)
+constexpr int kThreadsDec = 32 * kWarpsC;
+constexpr int kDepth = 3;                  // stages per warp
+constexpr int kStages = kWarpsC * kDepth;  // 24 stages of 8 KB
+constexpr int kStageBytes = 8192;          // one K tile + one V tile
 constexpr float kLn2f = 0.6931471805599453f;
 
 enum : int { kKvF16 = 0, kKvBF16 = 1, kKvE4M3 = 2 };
+
+// Keys per tile: a stage holds 4 KB of keys and 4 KB of values.
+constexpr int tile_keys(int D, int KV) { return 4096 / (D * (KV == kKvE4M3 ? 1 : 2)); }
 
 template <int D, int KV>
 struct DecCfg {
@@ -70,21 +74,13 @@ struct DecCfg {
   static constexpr int kBoxBytes = kRowBytes < 128 ? kRowBytes : 128;  // 128 (SW128) or 64 (SW64)
   static constexpr int kBoxCols = kBoxBytes / kEsz;
   static constexpr int kBoxes = kRowBytes / kBoxBytes;
-  static constexpr int kTileBytes = kTileKeys * kRowBytes;          // one K (or V) tile
-  static constexpr int kStageBytes = 2 * kTileBytes;                // K + V
-  // Tile t lives in stage t % kStages and is consumed by warp t % kWarpsC.
-  // With kStages a multiple of kWarpsC every stage belongs to one warp, so a
-  // warp waiting for tile t has itself consumed the stage's previous tile
-  // t - kStages: its barrier wait can never be two phases ahead (a parity wait
-  // two phases ahead would pass on the older phase and read a tile still in
-  // flight). Up to 192 KB of stages.
-  static constexpr int kStages = (196608 / kStageBytes) / kWarpsC * kWarpsC;
-  static_assert(kStages % kWarpsC == 0 && kStages >= kWarpsC, "stage ownership");
-  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kTK = tile_keys(D, KV);                      // 16, 32 or 64 keys
+  static constexpr int kTileBytes = kTK * kRowBytes;                // 4096: one K (or V) tile
+  static_assert(2 * kTileBytes == kStageBytes, "stage = K tile + V tile");
+  static constexpr int kRingBytes = kStages * kStageBytes;          // 192 KB
   static constexpr int kQOff = kRingBytes;                          // G*D floats (G <= 8)
   static constexpr int kBarOff = kQOff + 8 * D * 4;
-  static constexpr int kBtOff = kBarOff + 2 * kStages * 8 + 16;     // 2 x 32 block-table entries
-  static constexpr int kSmemBytes = kBtOff + 256 + 1024;
+  static constexpr int kSmemBytes = kBarOff + kStages * 8 + 16 + 1024;
 
   // Byte offset of byte `byte` of key row `row` inside a tile: 64-column
   // (128-byte) boxes one after another, rows 128 (or 64) bytes apart, the
@@ -93,7 +89,7 @@ struct DecCfg {
   static __device__ __forceinline__ int off(int row, int byte) {
     const int bx = byte / kBoxBytes, b = byte % kBoxBytes;
     const int sw = kBoxBytes == 128 ? (row & 7) : ((row >> 1) & 3);
-    return bx * (kTileKeys * kBoxBytes) + row * kBoxBytes + (((b >> 4) ^ sw) << 4) + (b & 15);
+    return bx * (kTK * kBoxBytes) + row * kBoxBytes + (((b >> 4) ^ sw) << 4) + (b & 15);
   }
 };
 
@@ -163,16 +159,6 @@ __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// 4-byte global -> shared copy that bypasses registers; src_bytes 0 writes zeros
-// and reads nothing.
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
 __device__ __forceinline__ uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
@@ -190,8 +176,8 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   float* sq = reinterpret_cast<float*>(smem + C::kQOff);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-  uint64_t* empty = full + C::kStages;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kBarOff + 2 * C::kStages * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kBarOff + kStages * 8);
+  constexpr int TK = C::kTK;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -209,13 +195,10 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   }
   const int64_t k0 = static_cast<int64_t>(split) * a.chunk;
   const int64_t k1 = (k0 + a.chunk < len) ? k0 + a.chunk : len;
-  const int ntiles = k1 > k0 ? static_cast<int>((k1 - k0 + kTileKeys - 1) / kTileKeys) : 0;
+  const int ntiles = k1 > k0 ? static_cast<int>((k1 - k0 + TK - 1) / TK) : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(full + s, 1);
-      mbar_init(empty + s, 1);
-    }
+    for (int s = 0; s < kStages; ++s) mbar_init(full + s, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -224,90 +207,64 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) sq[i] = to_float(qg[i]);
   __syncthreads();
 
-  if (warp == kWarpsC) {
-    // ------------------------------------------------------------ producer
-    // One lane waits and issues; the rest of the warp parks at the CTA
-    // barrier. (Polling the stage barriers from all 32 lanes, converged or
-    // not, slows the whole CTA by ~40 %.)
-    if (lane == 0) {
-      const int n_pc = kTileKeys / a.piece_rows;  // 1, 2 or 4 pieces per tile
-      // Block-table windows of 32 logical pages, double-buffered in shared
-      // memory and filled by cp.async one window ahead, so reading a page
-      // number never waits on global memory.
-      int32_t* bt_s = reinterpret_cast<int32_t*>(smem + C::kBtOff);
-      const int32_t* bt_row = a.block_table ? a.block_table + b * a.max_pages : nullptr;
-      auto bt_fill = [&](int w) {  // logical pages [w, w + 32) -> buffer (w / 32) % 2
-        int32_t* dst = bt_s + ((w >> 5) & 1) * 32;
-        for (int i = 0; i < 32; ++i) {
-          const int64_t idx = static_cast<int64_t>(w) + i;
-          const bool in = idx < a.max_pages;
-          cp_async4(dst + i, bt_row + (in ? idx : 0), in ? 4 : 0);
-        }
-        cp_async_commit();
-      };
-      int win = -1;
-      if (a.block_table && ntiles > 0) {
-        win = static_cast<int>(k0 / a.page_size) & ~31;
-        bt_fill(win);
-        bt_fill(win + 32);
-        cp_async_wait_group1();  // the first window has landed
+  // ------------------------------------------------------------ loading
+  // Warp w owns tiles t = w + 8 j (j = 0, 1, ...) and stages w, w + 8, w + 16:
+  // its j-th tile lands in stage w + 8 (j % 3). Each warp keeps its own three
+  // tiles in flight and refills a stage as soon as it has finished with it, so
+  // no warp ever waits for another (an in-order producer feeding all warps
+  // stalls behind the slowest one), and a stage's barrier is never waited on
+  // more than one phase ahead. Lane 0 issues the TMA copies.
+  // A paged cache's page numbers for the tile issued at the end of an
+  // iteration are loaded (one piece per lane) at its start, so the compute
+  // hides their latency.
+  const int n_own = ntiles > warp ? (ntiles - warp + kWarpsC - 1) / kWarpsC : 0;
+  const int n_pc = TK / a.piece_rows;  // pieces per tile: 1, 2, 4 or 8
+  auto tile_key0 = [&](int j) -> int32_t {
+    return static_cast<int32_t>(k0 + static_cast<int64_t>(warp + kWarpsC * j) * TK);
+  };
+  // Page of piece `lane` of own tile j (lanes >= n_pc: unused), -1 past the end.
+  auto load_page = [&](int j) -> int32_t {
+    if (!a.block_table || lane >= n_pc || j >= n_own) return -1;
+    const int32_t key = tile_key0(j) + lane * a.piece_rows;
+    if (key >= len) return -1;
+    const int32_t page = a.block_table[b * a.max_pages + key / a.page_size];
+    if (page < 0 || page >= a.num_pages) {
+      atomicExch(a.status, kStatusBadPage);
+      return -1;
+    }
+    return page;
+  };
+  auto issue = [&](int j, int32_t pg) {  // all lanes call; lane 0 issues
+    const int st = warp + kWarpsC * (j % kDepth);
+    uint8_t* base = smem + st * kStageBytes;
+    if (lane == 0) mbar_expect_tx(full + st, kStageBytes);
+    const int32_t key0 = tile_key0(j);
+    for (int p = 0; p < n_pc; ++p) {
+      const int32_t key = key0 + p * a.piece_rows;
+      int32_t page = static_cast<int32_t>(b), row = key;
+      if (a.block_table) {
+        page = __shfl_sync(0xffffffffu, pg, p);
+        row = key % a.page_size;
       }
-      int issued = 0;
-      for (int t = 0; t < ntiles; ++t) {
-        const int st = t % C::kStages;
-        if (!mbar_wait(empty + st, ((t / C::kStages) & 1) ^ 1, a.status, kStatusTimeoutFree, abort_flag)) break;
-        mbar_expect_tx(full + st, C::kStageBytes);
-        uint8_t* base = smem + st * C::kStageBytes;
-        const int32_t key0 = static_cast<int32_t>(k0 + static_cast<int64_t>(t) * kTileKeys);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          if (p >= n_pc) break;
-          const int32_t key = key0 + p * a.piece_rows;
-          int32_t page = static_cast<int32_t>(b), row = key;
-          if (a.block_table) {
-            const int32_t lp = key / a.page_size;  // logical page of this piece
-            row = key - lp * a.page_size;
-            const int w = lp & ~31;
-            if (w != win) {  // the next window (pieces advance by at most one page)
-              win = w;
-              bt_fill(w + 32);         // refill the buffer of the window just left
-              cp_async_wait_group1();  // window w (issued one window ago) has landed
-            }
-            page = bt_s[((w >> 5) & 1) * 32 + (lp - w)];
-            if (key >= len) {
-              page = -1;  // past the sequence end: the box reads as zeros
-            } else if (page < 0 || page >= a.num_pages) {
-              atomicExch(a.status, kStatusBadPage);
-              page = -1;
-            }
-          }
-          uint8_t* dst = base + p * a.piece_rows * C::kBoxBytes;
-          for (int bx = 0; bx < C::kBoxes; ++bx) {
-            tma_load_4d(dst + bx * (kTileKeys * C::kBoxBytes), &tk, full + st, bx * C::kBoxCols, row, kh, page);
-            tma_load_4d(dst + C::kTileBytes + bx * (kTileKeys * C::kBoxBytes), &tv, full + st, bx * C::kBoxCols,
-                        row, kh, page);
-          }
+      if (lane == 0) {
+        uint8_t* dst = base + p * a.piece_rows * C::kBoxBytes;
+        for (int bx = 0; bx < C::kBoxes; ++bx) {
+          tma_load_4d(dst + bx * (TK * C::kBoxBytes), &tk, full + st, bx * C::kBoxCols, row, kh, page);
+          tma_load_4d(dst + C::kTileBytes + bx * (TK * C::kBoxBytes), &tv, full + st, bx * C::kBoxCols, row,
+                      kh, page);
         }
-        issued = t + 1;
-      }
-      cp_async_wait_all();  // no copy into shared memory outlives the CTA
-      const int n = issued < C::kStages ? issued : C::kStages;
-      for (int s = 0; s < n; ++s) {
-        const int last = s + ((issued - 1 - s) / C::kStages) * C::kStages;
-        mbar_drain(full + s, (last / C::kStages) & 1);
       }
     }
-    __syncwarp();
-    __syncthreads();
-    return;
-  }
+  };
+  for (int j = 0; j < kDepth && j < n_own; ++j) issue(j, load_page(j));
+  int issued = n_own < kDepth ? n_own : kDepth;
 
   // -------------------------------------------------------------- compute
-  // Per 32-key tile, on tensor cores (m16n8k16, fp32 accumulators):
+  // Per tile of TK keys, on tensor cores (m16n8k16, fp32 accumulators):
   //   S   = Q K^T    M = 16 query rows (the G heads, zero-padded), N = 8 keys
-  //                  per n-tile (4 n-tiles), K = head dim;
+  //                  per n-tile (TK/8 n-tiles), K = head dim;
   //   O^T = V^T P^T  M = 16 value columns per m-tile (D/16 m-tiles), N = 8
-  //                  heads, K = 16 keys per step (2 steps).
+  //                  heads, K = 16 keys per step (TK/16 steps).
   // The S accumulator of a thread (head g = lane/4, keys 2c, 2c+1 of each
   // n-tile, c = lane%4) is exactly its B fragment of P^T, so P never leaves
   // registers. Softmax runs on the S accumulators; each thread's per-head
@@ -326,6 +283,8 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   constexpr bool kF8 = KV == kKvE4M3;
   constexpr int KS = D / 16;   // k-steps of Q K^T
   constexpr int MT = D / 16;   // m-tiles of P V
+  constexpr int NT = TK / 8;   // n-tiles of Q K^T
+  constexpr int PS = TK / 16;  // k-steps of P V
   const int g = lane >> 2, c = lane & 3;
   float sl2 = a.scale_log2;
   float qs = 1.f;
@@ -356,20 +315,23 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;
 
-  for (int t = warp; t < ntiles; t += kWarpsC) {
-    const int st = t % C::kStages;
-    bool ok = mbar_wait(full + st, (t / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag);
+  int consumed = 0;
+  for (int j = 0; j < n_own; ++j) {
+    const int st = warp + kWarpsC * (j % kDepth);
+    bool ok = mbar_wait(full + st, (j / kDepth) & 1, a.status, kStatusTimeoutLoad, abort_flag);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) break;
-    const uint8_t* kt = smem + st * C::kStageBytes;
+    consumed = j + 1;
+    const int32_t pg_next = load_page(j + kDepth);  // used after this tile's compute
+    const uint8_t* kt = smem + st * kStageBytes;
     const uint8_t* vt = kt + C::kTileBytes;
-    const int64_t tile0 = k0 + static_cast<int64_t>(t) * kTileKeys;
-    const int rem = static_cast<int>(k1 - tile0 < kTileKeys ? k1 - tile0 : kTileKeys);
+    const int64_t tile0 = k0 + static_cast<int64_t>(warp + kWarpsC * j) * TK;
+    const int rem = static_cast<int>(k1 - tile0 < TK ? k1 - tile0 : TK);
 
     // ---- S = Q K^T
-    float sacc[4][4];
+    float sacc[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
       if (kF8) {
         uint32_t kw[D / 16];
@@ -400,11 +362,11 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
     // ---- online softmax (head g; keys 8 nt + 2c + j)
     float mx = -INFINITY;
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float x = (8 * nt + 2 * c + j) < rem ? sacc[nt][j] * sl2 : -INFINITY;
-        sacc[nt][j] = x;
+      for (int e = 0; e < 2; ++e) {
+        const float x = (8 * nt + 2 * c + e) < rem ? sacc[nt][e] * sl2 : -INFINITY;
+        sacc[nt][e] = x;
         mx = fmaxf(mx, x);
       }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -413,9 +375,9 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
     const float alpha = ex2(m_run - m_new);
     m_run = m_new;
     float psum = 0.f;
-    uint32_t pb[2][2];  // B fragments of P^T for the two 16-key steps
+    uint32_t pb[PS][2];  // B fragments of P^T for the 16-key steps
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
+    for (int nt = 0; nt < NT; ++nt) {
       const float p0 = ex2(sacc[nt][0] - m_new), p1 = ex2(sacc[nt][1] - m_new);
       psum += p0 + p1;
       pb[nt >> 1][nt & 1] = pack_pair<kMmaBf16>(p0, p1);
@@ -433,7 +395,7 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
 
     // ---- O^T += V^T P^T
 #pragma unroll
-    for (int sp = 0; sp < 2; ++sp) {
+    for (int sp = 0; sp < PS; ++sp) {
       const int kb = 16 * sp;
       if (kF8) {
         constexpr int W = D / 32;  // 32-bit words of a thread's eighth of a value row
@@ -480,9 +442,19 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
         }
       }
     }
+    // Every lane has finished reading this stage: refill it with tile j + 3.
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty + st);
+    if (j + kDepth < n_own) {
+      issue(j + kDepth, pg_next);
+      issued = j + kDepth + 1;
+    }
   }
+  // After an abort, wait (bounded) for this warp's copies still in flight
+  // before the CTA reuses or releases the stages.
+  if (lane == 0)
+    for (int j = consumed; j < issued; ++j)
+      mbar_drain(full + warp + kWarpsC * (j % kDepth), (j / kDepth) & 1);
+  __syncwarp();
 
   // Per-thread sums -> per-head sums (the four threads of head g).
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
@@ -556,6 +528,7 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* ws_acc, 
 struct DecPlan {
   int64_t B, Hq, Hkv, S;
   int D, G, nsplit, chunk;
+  int tk;                       // keys per tile
   bool q_bf16;
   int kv;                       // kKvF16 / kKvBF16 / kKvE4M3
   int64_t page_size, num_pages, max_pages;
@@ -570,10 +543,10 @@ struct DecPlan {
 void split_keys(DecPlan* p) {
   const int64_t pairs = p->B * p->Hkv;
   const int64_t sms = sm_count();
-  const int64_t tiles = (p->S + kTileKeys - 1) / kTileKeys;
+  const int64_t tiles = (p->S + p->tk - 1) / p->tk;
   if (tiles == 0) {
     p->nsplit = 1;
-    p->chunk = kTileKeys;
+    p->chunk = p->tk;
     return;
   }
   int best = 1;
@@ -583,15 +556,15 @@ void split_keys(DecPlan* p) {
     const double waves = static_cast<double>(ctas) / sms;
     const double eff = waves / std::ceil(waves);
     // Prefer fewer splits unless a larger count fills waves clearly better;
-    // also keep at least 8 tiles per CTA so the ring pipelines.
-    if (tiles / ns < 8 && ns > 1) break;
+    // also keep at least 4 tiles per warp so each warp's pipeline fills.
+    if (tiles / ns < 4 * kWarpsC && ns > 1) break;
     if (eff > best_eff + 0.02) {
       best_eff = eff;
       best = ns;
     }
   }
   const int64_t per = (tiles + best - 1) / best;
-  p->chunk = static_cast<int>(per * kTileKeys);
+  p->chunk = static_cast<int>(per * p->tk);
   p->nsplit = static_cast<int>((p->S + p->chunk - 1) / p->chunk);
 }
 
@@ -601,7 +574,7 @@ pa_status check_shape(DecPlan* p) {
   const int64_t G = p->Hq / p->Hkv;
   if (G != 1 && G != 2 && G != 4 && G != 8) return fail(PA_ERR_UNSUPPORTED, "decode: group size must be 1, 2, 4 or 8");
   p->G = static_cast<int>(G);
-  if (p->S < 0 || p->S > 0x7fffffffLL - kTileKeys) return fail(PA_ERR_UNSUPPORTED, "decode: too many keys");
+  if (p->S < 0 || p->S > 0x7fffffffLL - 64) return fail(PA_ERR_UNSUPPORTED, "decode: too many keys");
   return PA_OK;
 }
 
@@ -622,6 +595,7 @@ pa_status make_plan(const pa_sdpa_desc& d, DecPlan* p) {
   PA_TRY(check_shape(p));
   p->q_bf16 = d.dtype == PA_BF16;
   p->kv = p->q_bf16 ? kKvBF16 : kKvF16;
+  p->tk = tile_keys(p->D, p->kv);
   p->page_size = d.S;
   p->num_pages = p->B;
   p->max_pages = 1;
@@ -629,7 +603,7 @@ pa_status make_plan(const pa_sdpa_desc& d, DecPlan* p) {
   p->head_stride = d.S * p->D;
   p->page_stride = Hkv * d.S * p->D;
   p->paged = false;
-  p->piece_rows = kTileKeys;
+  p->piece_rows = p->tk;
   p->scale = d.scale;
   p->k_scale = 1.f;
   p->v_scale = 1.f;
@@ -654,6 +628,7 @@ pa_status make_plan(const pa_kv_cache_desc& d, bool paged, DecPlan* p) {
   PA_TRY(check_shape(p));
   p->q_bf16 = d.q_dtype == PA_BF16;
   p->kv = d.kv_dtype == PA_FP8_E4M3 ? kKvE4M3 : (p->q_bf16 ? kKvBF16 : kKvF16);
+  p->tk = tile_keys(p->D, p->kv);
   p->page_size = d.page_size;
   p->num_pages = d.num_pages;
   p->max_pages = d.max_pages_per_seq;
@@ -672,13 +647,17 @@ pa_status make_plan(const pa_kv_cache_desc& d, bool paged, DecPlan* p) {
     if (d.page_size > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "decode: page_size too large");
     if (d.max_pages_per_seq < (d.max_seq_len + d.page_size - 1) / d.page_size)
       return fail(PA_ERR_INVALID, "decode: max_pages_per_seq * page_size must cover max_seq_len");
-    p->piece_rows = d.page_size % 32 == 0 ? 32 : (d.page_size % 16 == 0 ? 16 : 8);
+    // One TMA box per page piece: the largest power of two <= the tile that
+    // divides the page size (at least 8 rows).
+    int pr = p->tk;
+    while (d.page_size % pr) pr /= 2;
+    p->piece_rows = pr;
   } else {
     if (d.num_pages < d.batch) return fail(PA_ERR_INVALID, "decode: without a block table the cache needs one page per sequence");
     if (d.page_size < d.max_seq_len || d.page_size < 1 || d.page_size > 0x7fffffffLL)
       return fail(PA_ERR_INVALID, "decode: without a block table page_size must be at least max_seq_len");
     p->max_pages = 1;
-    p->piece_rows = kTileKeys;
+    p->piece_rows = p->tk;
   }
   split_keys(p);
   return PA_OK;
