@@ -26,6 +26,15 @@ torch.distributed provides only the barrier and the max-over-ranks timing.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle port of
 ``fused``) on the box's host cores on a bounded sample per step.
+
+KV-cache decode workloads (``--workload kv_fp8_decode_gqa``,
+``kv_paged_decode_gqa``, ``kv_paged_fp8_decode_gqa``) run the decode shapes
+(q (64, 32, 1, 128), caches for 64 sequences x 8 KV heads x 32768 keys) from
+an fp8 e4m3 cache and/or a paged cache (16-key pages in a seeded random
+order). ``value`` is GB/s of the bytes the kernel must read (cache in its
+storage type, block table, q) and write (out); ``e2e`` is a serving step:
+the query copied in from page-locked memory, the decode on the resident
+cache, the output copied back.
 """
 
 from __future__ import annotations
@@ -245,6 +254,8 @@ def run_reference(args):
         return 0
     from pa_b200 import workloads
 
+    if args.workload in KV_WORKLOADS:
+        return run_reference_kv(args)
     w = workloads.WORKLOADS[args.workload]
     rates = []
     for i in range(args.warmup + args.steps):
@@ -262,6 +273,27 @@ def run_reference(args):
         "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
                          "sample": desc + " per step; oracle port of the fused backend"},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_kv(args):
+    """The reference arm for the KV-cache workloads: the oracle's decode on whole sequences."""
+    rates = []
+    for i in range(args.warmup + args.steps):
+        rate, threads, desc = kv_cpu_sample(args.workload, budget_s=4.0)
+        if i >= args.warmup:
+            rates.append(rate)
+    value = statistics.median(rates)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic", "config": {"workload": args.workload + " (decode shapes, one sequence per item)"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": desc + " per step"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -606,6 +638,191 @@ def run_ring(args, rank, local, world, pg):
     return 0
 
 
+KV_WORKLOADS = {
+    "kv_fp8_decode_gqa": {"kv_format": "e4m3", "page_size": None},
+    "kv_paged_decode_gqa": {"kv_format": None, "page_size": 16},
+    "kv_paged_fp8_decode_gqa": {"kv_format": "e4m3", "page_size": 16},
+}
+
+
+_KV_SAMPLE: dict = {}
+
+
+def kv_cpu_sample(name, budget_s=12.0):
+    """The oracle's KV-cache decode (float64 restatement of the reference math on
+    the gathered, dequantised keys) on whole sequences of the workload's shape,
+    one thread per host core. Rate in GB/s of cache bytes in the storage type."""
+    from oracle.kvcache import decode_kv_reference, float_to_e4m3
+    from pa_b200 import workloads
+
+    spec = KV_WORKLOADS[name]
+    w = workloads.WORKLOADS["fp16_decode_gqa"]
+    _, hq, _, d = w.q_shape
+    _, hkv, s, _ = w.kv_shape
+    key = (name, hq, hkv, s, d)
+    if key not in _KV_SAMPLE:
+        gen = np.random.default_rng(3)
+        q = (gen.standard_normal((1, hq, d)) * 0.5).astype(np.float16)
+        k = (gen.standard_normal((1, hkv, s, d)) * 0.5).astype(np.float16)
+        v = (gen.standard_normal((1, hkv, s, d)) * 0.5).astype(np.float16)
+        if spec["kv_format"] == "e4m3":
+            k, v = float_to_e4m3(k), float_to_e4m3(v)
+        _KV_SAMPLE[key] = (q, k, v)
+    q, k, v = _KV_SAMPLE[key]
+    kw = {"kv_format": "e4m3"} if spec["kv_format"] == "e4m3" else {}
+    per_seq = 2 * k.nbytes
+    threads = os.cpu_count() or 1
+    done = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        while True:
+            list(ex.map(lambda _: decode_kv_reference(q, k, v, **kw), range(threads)))
+            done += threads
+            if time.perf_counter() - t0 > budget_s:
+                break
+    dt = time.perf_counter() - t0
+    return (done * per_seq / dt / 1e9, threads,
+            f"{done} sequences of q (1,{hq},{d}) vs a {hkv}x{s}x{d} cache, float64 oracle, {dt:.1f}s wall")
+
+
+def run_kvcache(args):
+    """Decode from an fp8 and/or paged KV cache (pa_decode_kv_fwd) on the decode shapes."""
+    rank, local, world, pg = dist_setup(args.gpus)
+    import torch
+
+    import pa_b200
+    from pa_b200 import workloads
+    from pa_b200._lib import check, lib
+    from pa_b200.device import DeviceBuffer, Event, Stream
+    from pa_b200.kvcache import kv_workspace_size
+
+    spec = KV_WORKLOADS[args.workload]
+    pa_b200.set_device(local)
+    dev = torch.device("cuda", local)
+    x = workloads.make("fp16_decode_gqa")
+    q = torch.from_numpy(np.ascontiguousarray(x["q"][:, :, 0])).to(dev)
+    k = torch.from_numpy(x["k"]).to(dev)
+    v = torch.from_numpy(x["v"]).to(dev)
+    del x
+    B, Hq, D = q.shape
+    Hkv, S = k.shape[1], k.shape[2]
+    if spec["kv_format"] == "e4m3":
+        k = k.to(torch.float8_e4m3fn).view(torch.uint8)
+        v = v.to(torch.float8_e4m3fn).view(torch.uint8)
+    table = None
+    ps = spec["page_size"]
+    if ps:
+        n_pages = B * S // ps
+        gen = torch.Generator(device=dev).manual_seed(7)
+        perm = torch.randperm(n_pages, device=dev, generator=gen)
+
+        def to_pages(t):
+            tp = t.view(B, Hkv, S // ps, ps, D).permute(0, 2, 1, 3, 4).reshape(n_pages, Hkv, ps, D)
+            out = torch.empty_like(tp)
+            out[perm] = tp
+            return out
+
+        k, v = to_pages(k), to_pages(v)
+        table = perm.view(B, S // ps).to(torch.int32).contiguous()
+    torch.cuda.synchronize(dev)
+    desc = pa_b200.kv_cache_desc(B, Hq, D, tuple(k.shape), kv_format=spec["kv_format"],
+                                 paged=table is not None,
+                                 max_pages_per_seq=table.shape[1] if table is not None else 0,
+                                 max_seq_len=S)
+    ws_bytes = kv_workspace_size(desc, table is not None)
+    ws = DeviceBuffer(ws_bytes)
+    out = torch.empty_like(q)
+    stream = Stream()
+
+    def step():
+        pa_b200.decode_kv_device(desc, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                 block_table_ptr=None if table is None else table.data_ptr(),
+                                 stream=stream, workspace=(ws.ptr, ws_bytes))
+
+    out_dir = ROOT / "gpurun_out"
+    out_dir.mkdir(exist_ok=True)
+    clocks = ClockSampler(local, out_dir / f"clocks_rank{rank}.csv").start()
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    pa_b200.sync_device_status()
+    events = [Event() for _ in range(args.steps + 1)]
+    barrier(pg)
+    stream.synchronize()
+    clocks.mark(0)
+    events[0].record(stream)
+    for i in range(args.steps):
+        step()
+        events[i + 1].record(stream)
+    stream.synchronize()
+    clocks.mark(1)
+    clocks.stop()
+    barrier(pg)
+    pa_b200.sync_device_status()
+    per = [events[i].elapsed_ms(events[i + 1]) for i in range(args.steps)]
+    ms = max_over_ranks(pg, events[0].elapsed_ms(events[-1]) / args.steps, local)
+    work = float(2 * k.numel() * k.element_size() + 2 * q.numel() * q.element_size()
+                 + (table.numel() * 4 if table is not None else 0))
+    value = world * work / (ms * 1e-3) / 1e9
+    pk, pk_kind = peaks()
+    achieved = work / (statistics.mean(per) * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"], "traffic": traffic_for(args.workload),
+            "peak_kind": pk_kind, "kernel": "decode_partial + decode_combine"}
+
+    # Serving step end to end: the query in from page-locked memory, decode on the
+    # resident cache, the output back (synchronous per step).
+    hq_in = pa_b200.pinned_empty((B, Hq, D), np.float16)
+    hq_in[...] = q.cpu().numpy()
+    h_out = pa_b200.pinned_empty((B, Hq, D), np.float16)
+    for _ in range(3):
+        check(lib().pa_memcpy_h2d(q.data_ptr(), hq_in.ctypes.data, hq_in.nbytes, stream.handle))
+        step()
+        check(lib().pa_memcpy_d2h(h_out.ctypes.data, out.data_ptr(), h_out.nbytes, stream.handle))
+        stream.synchronize()
+    e2e_steps = max(1, min(args.steps, 20))
+    barrier(pg)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        check(lib().pa_memcpy_h2d(q.data_ptr(), hq_in.ctypes.data, hq_in.nbytes, stream.handle))
+        step()
+        check(lib().pa_memcpy_d2h(h_out.ctypes.data, out.data_ptr(), h_out.nbytes, stream.handle))
+        stream.synchronize()
+    e2e_ms = max_over_ranks(pg, (time.perf_counter() - t0) * 1e3 / e2e_steps, local)
+    pa_b200.sync_device_status()
+    if rank != 0:
+        if pg is not None:
+            pg.destroy_process_group()
+        return 0
+    cache = f"{'fp8 e4m3' if spec['kv_format'] else 'fp16'} {'paged (16-key pages, random order)' if ps else 'contiguous'}"
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3 cache, f16 q/out" if spec["kv_format"] else "f16",
+        "data": "synthetic",
+        "config": {"workload": f"{args.workload}: q ({B}, {Hq}, 1, {D}) vs a {cache} cache of "
+                               f"{B} sequences x {Hkv} kv heads x {S} keys x {D}",
+                   "global_batch": B * world, "seq_len": S,
+                   "parallelism": f"batch-shard x{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (no flush)"},
+        "roofline": roof,
+        "e2e": {"value": world * work / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": int(hq_in.nbytes) * world,
+                "d2h_bytes_per_step": int(h_out.nbytes) * world, "ms_per_step": e2e_ms,
+                "timing": "host wall clock; cache resident on the device, query in and output out per step"},
+        "gpu_launches": args.steps * 2,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        rate, threads, desc_s = kv_cpu_sample(args.workload)
+        line["cpu_baseline"] = {"value": rate, "unit": "GB/s", "cores": threads, "kind": "port",
+                                "sample": desc_s}
+    print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
 def traffic_for(name):
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
@@ -630,6 +847,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload in KV_WORKLOADS:
+        return run_kvcache(args)
     return run_gpu(args)
 
 

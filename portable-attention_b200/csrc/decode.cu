@@ -371,7 +371,12 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
       }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m_run, mx);  // finite: the tile has >= 1 valid key
+    // The running max moves only when a score exceeds it by more than 2^8
+    // (p <= 256 stays exact enough in f16/bf16 and fp32 sums), so after the
+    // first tiles the accumulators are rarely rescaled; mx is finite because
+    // the tile has at least one valid key.
+    const bool moved = mx > m_run + 8.f;
+    const float m_new = moved ? mx : m_run;
     const float alpha = ex2(m_run - m_new);
     m_run = m_new;
     float psum = 0.f;
@@ -383,14 +388,16 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
       pb[nt >> 1][nt & 1] = pack_pair<kMmaBf16>(p0, p1);
     }
     l_run = l_run * alpha + psum;
-    const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * c);      // head 2c
-    const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);  // head 2c + 1
+    if (__any_sync(0xffffffffu, moved)) {
+      const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * c);      // head 2c
+      const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);  // head 2c + 1
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      o[mt][0] *= al0;
-      o[mt][1] *= al1;
-      o[mt][2] *= al0;
-      o[mt][3] *= al1;
+      for (int mt = 0; mt < MT; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+      }
     }
 
     // ---- O^T += V^T P^T
