@@ -13,9 +13,10 @@
 //               softmax overlaps the other tile's tensor-core work.
 // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,256+D), O1 after.
 //
-// Softmax per key tile: the row max is taken on raw scores (scale > 0), each
-// probability costs one FFMA and one ex2, partial max/sum chains are split
-// eight ways for ILP, and P is packed to fp16/bf16 into the first 64 columns
+// Softmax per key tile: the row max is taken on raw scores (scale > 0) with
+// three-input maxima, each pair of probabilities costs one packed f32x2 FMA,
+// two ex2 and one packed add, partial max/sum chains are split for ILP, and
+// P is packed to fp16/bf16 into the first 64 columns
 // of its S buffer (aliasing S). The running max moves only when it grows by
 // more than 2^8 (log2 units), so O is rescaled rarely. Fully-masked rows keep
 // l = 0 and produce exact zeros and lse = -inf.
@@ -494,34 +495,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // Row max of raw scores (scale > 0), eight partial chains.
+      // Row max of raw scores (scale > 0): eight chains of three-input maxima.
       float mx8[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mx8[u] = x[u];
+      for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(x[2 * u], x[2 * u + 1]);
 #pragma unroll
-      for (int u = 8; u < BN; ++u) mx8[u & 7] = fmaxf(mx8[u & 7], x[u]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
+      for (int u = 16; u < BN; u += 2) mx8[(u >> 1) & 7] = max3(mx8[(u >> 1) & 7], x[u], x[u + 1]);
+      const float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) * sl2;
       const float m_new = fmaxf(m_run, mx);
       const float m_use = (m_run == -INFINITY || m_new - m_run > kRescaleSlack) ? m_new : m_run;
       const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
-      float sum8[8];
+      // p = 2^(x * scale - m), two columns per packed FMA and packed add.
+      const uint64_t sl2x2 = f2(sl2, sl2), negm2 = f2(neg_m, neg_m);
+      uint64_t sum4[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) sum8[u] = 0.f;
+      for (int u = 0; u < 4; ++u) sum4[u] = 0ull;
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float p0 = ex2(fmaf(x[c * 32 + 2 * u], sl2, neg_m));
-          const float p1 = ex2(fmaf(x[c * 32 + 2 * u + 1], sl2, neg_m));
-          sum8[u & 7] += p0 + p1;
+          const uint64_t y = fma2(f2(x[c * 32 + 2 * u], x[c * 32 + 2 * u + 1]), sl2x2, negm2);
+          const float p0 = ex2(f2_lo(y));
+          const float p1 = ex2(f2_hi(y));
+          sum4[u & 3] = add2(sum4[u & 3], f2(p0, p1));
           pk[u] = pack2(p0, p1, BF16);
         }
         tmem_st16(s_addr + c * 16, pk);
       }
       tmem_st_wait();
-      const float rowsum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      const uint64_t s2 = add2(add2(sum4[0], sum4[1]), add2(sum4[2], sum4[3]));
+      const float rowsum = f2_lo(s2) + f2_hi(s2);
       const float alpha = (m_use == m_run) ? 1.f : ((m_run == -INFINITY) ? 0.f : ex2(m_run - m_use));
       const bool need = (icnt > 0) && (m_use != m_run);
       if (__any_sync(0xffffffffu, need)) {
@@ -535,8 +539,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(o_addr + c * 32, rr);
           tmem_ld_wait();
           reg_fence(rr);
+          const uint64_t al2 = f2(alpha, alpha);
 #pragma unroll
-          for (int u = 0; u < 32; ++u) rr[u] = __float_as_uint(__uint_as_float(rr[u]) * alpha);
+          for (int u = 0; u < 16; ++u) {
+            const uint64_t y = mul2(f2(__uint_as_float(rr[2 * u]), __uint_as_float(rr[2 * u + 1])), al2);
+            rr[2 * u] = __float_as_uint(f2_lo(y));
+            rr[2 * u + 1] = __float_as_uint(f2_hi(y));
+          }
           tmem_st32(o_addr + c * 32, rr);
         }
         tmem_st_wait();
