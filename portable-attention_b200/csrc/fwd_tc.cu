@@ -45,7 +45,16 @@ constexpr int kTiles = 2;
 constexpr int kSoftWarps = 4 * kTiles;
 constexpr int kProducerWarp = kSoftWarps;
 constexpr int kMmaWarp = kSoftWarps + 1;
-constexpr int kThreads = 32 * (kSoftWarps + 2);
+// Warpgroup 2 holds the producer (warp 8) and MMA (warp 9) warps and two
+// idle warps: registers are allocated per warpgroup, so a 10-warp CTA would
+// pay for 12 anyway, and whole warpgroups can move registers with setmaxnreg.
+constexpr int kThreads = 32 * 12;
+// Register split (setmaxnreg): the softmax warpgroups keep a 128-column score
+// row per thread; the producer/MMA warpgroup needs few. 128 x (2 x 200 + 80)
+// = 61440 registers, at most the 384 x 160 a launch of >= 160 registers per
+// thread provides (checked on the host before the first launch).
+constexpr int kRegsSoft = 200;
+constexpr int kRegsOther = 80;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleSlack = 8.0f;
@@ -281,7 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  if (warp >= kSoftWarps) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -423,7 +433,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(mma_done, 0);
     }
     __syncwarp();
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoft));
     // --------------------------------------------------------------- softmax
     const int t = warp / 4;                 // query tile of this warpgroup
     const int quad = warp & 3;
@@ -607,6 +619,17 @@ pa_status launch_variant(const CUtensorMap& tq, const CUtensorMap& tk, const CUt
   constexpr int smem = TcCfg<D>::kSmemBytes;
   static uint64_t attr_set = 0;  // one bit per device
   PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, &attr_set));
+  // setmaxnreg.inc waits until the pool of registers the CTA was launched
+  // with can cover the request: never launch a build whose per-thread count
+  // is too small for the split (it would wait forever).
+  static int regs = 0;
+  if (regs == 0) {
+    cudaFuncAttributes fa{};
+    PA_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(kern)));
+    regs = fa.numRegs;
+  }
+  if (regs * kThreads < 128 * (2 * kRegsSoft + kRegsOther))
+    return fail(PA_ERR_UNSUPPORTED, "fwd_tc: kernel built with too few registers for its register split");
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(tq, tk, tv, a);
   PA_CUDA(cudaGetLastError());
   return PA_OK;
