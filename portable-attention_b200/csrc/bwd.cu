@@ -33,7 +33,11 @@
 namespace pa {
 namespace {
 
-constexpr int kThreadsB = 192;
+// Warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 two "softmax" warpgroups
+// that split each block's 64 columns in halves (thread <-> TMEM lane <-> row;
+// there is no row reduction in the backward, so the halves are independent).
+constexpr int kThreadsB = 320;
+constexpr int kSoftThreadsB = 256;
 constexpr int kRowPad = 64;
 
 struct BwdArgs {
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(sdp_full + s, 1);
-      mbar_init(ds_ready + s, 128);
+      mbar_init(ds_ready + s, kSoftThreadsB);
     }
     mbar_init(acc_done, 1);
     mbar_init(mma_done, 1);
@@ -280,6 +284,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     __syncwarp();
   } else {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // which 32 columns of each block this warpgroup owns
     const int r = quad * 32 + lane;
     const int64_t key = n0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -301,8 +306,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       const int64_t hi = a.L - q0;
       const int cmax = static_cast<int>(hi < 0 ? 0 : (hi > BQ ? BQ : hi));
       const bool all_vis = __all_sync(0xffffffffu, cmin == 0 && cmax == BQ);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      {
         uint32_t sr[32], pr[32];
         tmem_ld32(lane_base + C::kColS + sb * 64 + half * 32, sr);
         tmem_ld32(lane_base + C::kColP + sb * 64 + half * 32, pr);
@@ -310,27 +314,35 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         reg_fence(sr);
         reg_fence(pr);
         uint32_t pk[16], dk[16];
+        const uint64_t sl2x2 = f2(a.scale_log2, a.scale_log2);
 #pragma unroll
         for (int v4 = 0; v4 < 8; ++v4) {
           const float4 lz = reinterpret_cast<const float4*>(l2)[half * 8 + v4];
           const float4 dd = reinterpret_cast<const float4*>(dl)[half * 8 + v4];
+          const uint64_t nlz[2] = {f2(-lz.x, -lz.y), f2(-lz.z, -lz.w)};
+          const uint64_t ndd[2] = {f2(-dd.x, -dd.y), f2(-dd.z, -dd.w)};
           const float lzv[4] = {lz.x, lz.y, lz.z, lz.w};
-          const float ddv[4] = {dd.x, dd.y, dd.z, dd.w};
-          float p4[4], d4[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int e = v4 * 4 + u;          // column inside this half
+          for (int w = 0; w < 2; ++w) {
+            const int e = v4 * 4 + 2 * w;      // column pair inside this half
             const int c = half * 32 + e;       // column inside the block
-            float p = ex2(fmaf(__uint_as_float(sr[e]), a.scale_log2, -lzv[u]));
-            if (!all_vis) p = (c >= cmin && c < cmax && lzv[u] != -INFINITY) ? p : 0.f;
-            p4[u] = p;
-            d4[u] = p * (__uint_as_float(pr[e]) - ddv[u]);
-            if (!all_vis && !(c >= cmin && c < cmax)) d4[u] = 0.f;
+            // p = 2^(s * scale - lse), dS = p * (dP - delta), two columns at a time
+            const uint64_t y = fma2(f2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), sl2x2, nlz[w]);
+            float p0 = ex2(f2_lo(y)), p1 = ex2(f2_hi(y));
+            if (!all_vis) {
+              p0 = (c >= cmin && c < cmax && lzv[2 * w] != -INFINITY) ? p0 : 0.f;
+              p1 = (c + 1 >= cmin && c + 1 < cmax && lzv[2 * w + 1] != -INFINITY) ? p1 : 0.f;
+            }
+            const uint64_t p2 = f2(p0, p1);
+            const uint64_t d2 = mul2(p2, add2(f2(__uint_as_float(pr[e]), __uint_as_float(pr[e + 1])), ndd[w]));
+            float d0 = f2_lo(d2), d1 = f2_hi(d2);
+            if (!all_vis) {
+              if (!(c >= cmin && c < cmax)) d0 = 0.f;
+              if (!(c + 1 >= cmin && c + 1 < cmax)) d1 = 0.f;
+            }
+            pk[v4 * 2 + w] = pack2(p0, p1, BF16);
+            dk[v4 * 2 + w] = pack2(d0, d1, BF16);
           }
-          pk[v4 * 2] = pack2(p4[0], p4[1], BF16);
-          pk[v4 * 2 + 1] = pack2(p4[2], p4[3], BF16);
-          dk[v4 * 2] = pack2(d4[0], d4[1], BF16);
-          dk[v4 * 2 + 1] = pack2(d4[2], d4[3], BF16);
         }
         tmem_st16(lane_base + C::kColS + sb * 64 + half * 16, pk);
         tmem_st16(lane_base + C::kColP + sb * 64 + half * 16, dk);
@@ -349,7 +361,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       uint8_t* dvrow = static_cast<uint8_t*>(a.dv) + ((pair * a.S + key) * D) * 2;
       uint8_t* dkrow = static_cast<uint8_t*>(a.dk) + ((pair * a.S + key) * D) * 2;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
         uint32_t rv[32], rk[32];
         if (n > 0) {
           tmem_ld32(lane_base + C::kColV + c * 32, rv);
@@ -438,7 +450,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(sdp_full + s, 1);
-      mbar_init(ds_ready + s, 128);
+      mbar_init(ds_ready + s, kSoftThreadsB);
     }
     mbar_init(acc_done, 1);
     mbar_init(mma_done, 1);
@@ -536,6 +548,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     __syncwarp();
   } else {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // which 32 columns of each block this warpgroup owns
     const int r = quad * 32 + lane;
     const int64_t row = m0 + r;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -554,8 +567,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       const int64_t lim64 = row_live ? vis - k0 : 0;
       const int lim = static_cast<int>(lim64 < 0 ? 0 : (lim64 > BK ? BK : lim64));
       const bool all_vis = __all_sync(0xffffffffu, lim == BK);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      {
         uint32_t sr[32], pr[32];
         tmem_ld32(lane_base + C::kColS + sb * 64 + half * 32, sr);
         tmem_ld32(lane_base + C::kColP + sb * 64 + half * 32, pr);
@@ -563,18 +575,20 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         reg_fence(sr);
         reg_fence(pr);
         uint32_t dk[16];
+        const uint64_t sl2x2 = f2(a.scale_log2, a.scale_log2), nlz = f2(-lz, -lz), ndl = f2(-dlt, -dlt);
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          float d2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = half * 32 + 2 * t + u;
-            const float p = ex2(fmaf(__uint_as_float(sr[2 * t + u]), a.scale_log2, -lz));
-            float d = p * (__uint_as_float(pr[2 * t + u]) - dlt);
-            if (!all_vis && c >= lim) d = 0.f;
-            d2[u] = d;
+          const int c = half * 32 + 2 * t;
+          // p = 2^(s * scale - lse), dS = p * (dP - delta), two columns at a time
+          const uint64_t y = fma2(f2(__uint_as_float(sr[2 * t]), __uint_as_float(sr[2 * t + 1])), sl2x2, nlz);
+          const uint64_t p2 = f2(ex2(f2_lo(y)), ex2(f2_hi(y)));
+          const uint64_t d2 = mul2(p2, add2(f2(__uint_as_float(pr[2 * t]), __uint_as_float(pr[2 * t + 1])), ndl));
+          float d0 = f2_lo(d2), d1 = f2_hi(d2);
+          if (!all_vis) {
+            if (c >= lim) d0 = 0.f;
+            if (c + 1 >= lim) d1 = 0.f;
           }
-          dk[t] = pack2(d2[0], d2[1], BF16);
+          dk[t] = pack2(d0, d1, BF16);
         }
         tmem_st16(lane_base + C::kColP + sb * 64 + half * 16, dk);
       }
@@ -590,7 +604,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       tc_fence_after();
       uint8_t* dqrow = static_cast<uint8_t*>(a.dq) + ((zq * a.L + row) * D) * 2;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
         uint32_t rq[32];
         if (n > 0) {
           tmem_ld32(lane_base + C::kColQ + c * 32, rq);
