@@ -700,9 +700,10 @@ def run_kvcache(args):
     pa_b200.set_device(local)
     dev = torch.device("cuda", local)
     x = workloads.make("fp16_decode_gqa")
-    q = torch.from_numpy(np.ascontiguousarray(x["q"][:, :, 0])).to(dev)
-    k = torch.from_numpy(x["k"]).to(dev)
-    v = torch.from_numpy(x["v"]).to(dev)
+    rows = slice(0, args.batch) if args.batch else slice(None)   # --batch: the first sequences only
+    q = torch.from_numpy(np.ascontiguousarray(x["q"][rows, :, 0])).to(dev)
+    k = torch.from_numpy(np.ascontiguousarray(x["k"][rows])).to(dev)
+    v = torch.from_numpy(np.ascontiguousarray(x["v"][rows])).to(dev)
     del x
     B, Hq, D = q.shape
     Hkv, S = k.shape[1], k.shape[2]
