@@ -257,6 +257,27 @@ pa_status pa_decode_fwd_static(const pa_sdpa_desc* desc, const void* q, const vo
                                void* stream);
 
 /*
+ * The tile plan the tensor-core forward compiles for a head dimension and
+ * element size (pa_sdpa_fwd's fwd_tc kernel), in the vocabulary of the
+ * reference's tile planner (tiling.py:68-121 DeviceLimits / :125-145
+ * TilePlan): rows per query tile and keys per streamed tile, threads and
+ * shared memory per CTA, plus what tcgen05 adds (query tiles per CTA, K/V
+ * stages, TMEM columns). Returns PA_ERR_UNSUPPORTED for shapes the kernel
+ * does not take (they run on the exact CUDA-core kernel).
+ */
+typedef struct pa_tile_plan {
+  int32_t block_q;          /* query rows per tile */
+  int32_t block_k;          /* keys per streamed K/V tile */
+  int32_t query_tiles;      /* query tiles per CTA */
+  int32_t threads;          /* threads per CTA */
+  int32_t shared_memory_bytes;
+  int32_t tmem_columns;
+  int32_t k_stages, v_stages;
+} pa_tile_plan;
+
+pa_status pa_fwd_tile_plan(int32_t head_dim, int32_t dtype_bytes, pa_tile_plan* plan);
+
+/*
  * Backward (VJP) of pa_sdpa_fwd: dQ, dK, dV from q, k, v, the forward output,
  * its cotangent dout and the forward's lse. The reference has no backward
  * (the autograd hook is a roadmap item, ROADMAP.md:57-58); this is the

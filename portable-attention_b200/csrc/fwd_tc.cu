@@ -757,3 +757,33 @@ pa_status launch_fwd_tc(const pa_sdpa_desc& d, const void* q, const void* k, con
 }
 
 }  // namespace pa
+
+namespace {
+template <int D>
+void fill_plan(pa_tile_plan* p) {
+  using C = pa::TcCfg<D>;
+  p->block_q = pa::BM;
+  p->block_k = pa::BN;
+  p->query_tiles = pa::kTiles;
+  p->threads = pa::kThreads;
+  p->shared_memory_bytes = C::kSmemBytes;
+  p->tmem_columns = static_cast<int32_t>(pa::kTmemCols);
+  p->k_stages = C::kKStages;
+  p->v_stages = C::kVStages;
+}
+}  // namespace
+
+extern "C" pa_status pa_fwd_tile_plan(int32_t head_dim, int32_t dtype_bytes, pa_tile_plan* plan) {
+  pa::clear_error();
+  if (!plan) return pa::fail(PA_ERR_INVALID, "null plan");
+  if (dtype_bytes != 2) return pa::fail(PA_ERR_UNSUPPORTED, "the tensor-core forward takes 2-byte elements (fp16/bf16)");
+  if (head_dim == 128) {
+    fill_plan<128>(plan);
+    return PA_OK;
+  }
+  if (head_dim == 64) {
+    fill_plan<64>(plan);
+    return PA_OK;
+  }
+  return pa::fail(PA_ERR_UNSUPPORTED, "the tensor-core forward takes head_dim 64 or 128");
+}

@@ -23,11 +23,12 @@ from .kvcache import decode_kv_cache, decode_kv_device, kv_cache_desc
 from .device import (DeviceBuffer, Event, Stream, current_device, device_count, pinned_empty,
                      set_device, sync_device_status)
 from .plan import compute_dtype, plan_call
+from .tiling import B200_LIMITS, plan_tcgen05_tiles
 
 __all__ = [
-    "DeviceBuffer", "Event", "LibraryError", "PaError", "Stream", "available", "compute_dtype",
+    "B200_LIMITS", "DeviceBuffer", "Event", "LibraryError", "PaError", "Stream", "available", "compute_dtype",
     "current_device", "decode_kv_cache", "decode_kv_device", "device_count", "forward_with_lse",
-    "kv_cache_desc", "library_path", "pinned_empty",
+    "kv_cache_desc", "library_path", "plan_tcgen05_tiles", "pinned_empty",
     "plan_call", "register", "scaled_dot_product_attention", "sdpa_backward", "sdpa_device",
     "set_device", "sync_device_status",
 ]
