@@ -257,6 +257,24 @@ pa_status pa_decode_fwd_static(const pa_sdpa_desc* desc, const void* q, const vo
                                void* stream);
 
 /*
+ * One forward call spread over several GPUs of this process (batch x head
+ * sharding; no reference counterpart: the reference runs one CPU call).
+ * `desc` describes HOST operands exactly as for pa_sdpa_fwd; q, k, v, mask,
+ * out and lse are host pointers (page-locked memory copies fastest). The
+ * first leading dimension is cut into contiguous shards, one per entry of
+ * `devices` (fewer if it has fewer indices); each device copies its rows in,
+ * runs the same kernels as pa_sdpa_fwd (or the split-KV decode for L == 1)
+ * and copies its rows of out / lse back, driven by its own host thread.
+ * Operands broadcast over the first dimension (stride 0, e.g. a mask) are
+ * copied whole to every device. When the first dimension is the grouped-
+ * query head axis, shards hold whole groups. Blocks until every device has
+ * finished; the first failure is returned with the device named.
+ */
+pa_status pa_shard_fwd(int32_t ndev, const int32_t* devices, const pa_sdpa_desc* desc,
+                       const void* q, const void* k, const void* v, const void* mask, void* out,
+                       float* lse);
+
+/*
  * The tile plan the tensor-core forward compiles for a head dimension and
  * element size (pa_sdpa_fwd's fwd_tc kernel), in the vocabulary of the
  * reference's tile planner (tiling.py:68-121 DeviceLimits / :125-145

@@ -23,4 +23,10 @@ pa_status launch_fill_dead(const pa_sdpa_desc& d, void* out, float* lse, cudaStr
 // leading axis; reports the flattened slice count and head counts.
 bool dense_bhsd(const pa_sdpa_desc& d, int64_t* slices, int64_t* heads, int64_t* kv_heads);
 
+// Split-KV decode (query length 1) on dense operands: workspace size, and a
+// run with a caller-provided workspace (csrc/decode.cu).
+pa_status decode_ws_bytes(const pa_sdpa_desc& d, size_t* bytes);
+pa_status run_decode(const pa_sdpa_desc& d, const void* q, const void* k, const void* v, void* out,
+                     float* lse, void* ws, size_t ws_bytes, cudaStream_t st);
+
 }  // namespace pa

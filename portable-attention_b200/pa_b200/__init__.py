@@ -18,7 +18,7 @@ from __future__ import annotations
 
 from ._lib import LibraryError, PaError, library_path
 from .autograd import forward_with_lse, sdpa_backward
-from .backend import scaled_dot_product_attention, sdpa_device
+from .backend import scaled_dot_product_attention, sdpa_device, sdpa_sharded
 from .kvcache import decode_kv_cache, decode_kv_device, kv_cache_desc
 from .device import (DeviceBuffer, Event, Stream, current_device, device_count, pinned_empty,
                      set_device, sync_device_status)
@@ -29,7 +29,7 @@ __all__ = [
     "B200_LIMITS", "DeviceBuffer", "Event", "LibraryError", "PaError", "Stream", "available", "compute_dtype",
     "current_device", "decode_kv_cache", "decode_kv_device", "device_count", "forward_with_lse",
     "kv_cache_desc", "library_path", "plan_tcgen05_tiles", "pinned_empty",
-    "plan_call", "register", "scaled_dot_product_attention", "sdpa_backward", "sdpa_device",
+    "plan_call", "register", "scaled_dot_product_attention", "sdpa_backward", "sdpa_device", "sdpa_sharded",
     "set_device", "sync_device_status",
 ]
 

@@ -134,6 +134,7 @@ SIGNATURES = {
     "pa_decode_kv_workspace_size": [ctypes.POINTER(KvCacheDesc), _I32, ctypes.POINTER(ctypes.c_size_t)],
     "pa_decode_kv_fwd": [ctypes.POINTER(KvCacheDesc), _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     "pa_fwd_tile_plan": [_I32, _I32, _P],
+    "pa_shard_fwd": [_I32, _P, _DESC, _P, _P, _P, _P, _P, _P],
     "pa_sdpa_bwd": [_DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "pa_comm_unique_id": [ctypes.c_char_p],
     "pa_comm_init": [ctypes.POINTER(_P), ctypes.c_char_p, _I32, _I32],

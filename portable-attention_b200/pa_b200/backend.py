@@ -26,7 +26,7 @@ from .device import DeviceArena, Event, Stream, pinned_empty, sync_device_status
 from .plan import plan_call
 from .validation import validate
 
-__all__ = ["scaled_dot_product_attention", "sdpa_device", "use_decode_kernel"]
+__all__ = ["scaled_dot_product_attention", "sdpa_device", "sdpa_sharded", "use_decode_kernel"]
 
 _state = threading.local()
 _arenas: dict[int, DeviceArena] = {}
@@ -171,6 +171,43 @@ def scaled_dot_product_attention(query, key, value, attn_mask=None, dropout_p=0.
             _run_pipelined(plan, host, mask, out, (dq, dk, dv, dm, do), n_chunks, query, key,
                            value, attn_mask, is_causal, scale, group, st)
     sync_device_status()
+    return out.astype(query.dtype, copy=False)
+
+
+def sdpa_sharded(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, *, scale=None,
+                 enable_gqa=False, devices=None):
+    """The same call as :func:`scaled_dot_product_attention`, spread over several GPUs.
+
+    The first leading dimension is cut into one contiguous shard per device
+    (``devices``: CUDA device indices, default every visible device) through
+    ``pa_shard_fwd``; each device copies in its rows, runs the same kernels
+    and copies its rows of the result back, driven by its own host thread.
+    Results are identical to the single-GPU call.
+    """
+    from .device import device_count
+
+    group = validate(query, key, value, attn_mask, dropout_p, is_causal, enable_gqa)
+    plan = plan_call(query.shape, key.shape, value.shape, query.dtype, key.dtype, value.dtype,
+                     None if attn_mask is None else np.shape(attn_mask),
+                     None if attn_mask is None else np.asarray(attn_mask).dtype,
+                     is_causal, scale, group)
+    cdt = plan.cdt
+    host = [np.ascontiguousarray(x, dtype=cdt) for x in (query, key, value)]
+    mask = None
+    if plan.mask_kind != PA_MASK_NONE:
+        m = np.asarray(attn_mask).reshape(plan.mask_shape)
+        mask = (np.ascontiguousarray(m).view(np.uint8) if m.dtype == np.bool_
+                else np.ascontiguousarray(m, dtype=plan.mask_host_dtype))
+    out = np.empty(plan.out_shape, dtype=cdt)
+    if out.size == 0:
+        return out.astype(query.dtype, copy=False)
+    devs = list(range(device_count())) if devices is None else [int(x) for x in devices]
+    if not devs:
+        raise ValueError("sdpa_sharded: no CUDA device to run on")
+    arr = (ctypes.c_int32 * len(devs))(*devs)
+    check(lib().pa_shard_fwd(len(devs), arr, ctypes.byref(plan.desc), host[0].ctypes.data,
+                             host[1].ctypes.data, host[2].ctypes.data,
+                             mask.ctypes.data if mask is not None else None, out.ctypes.data, None))
     return out.astype(query.dtype, copy=False)
 
 
