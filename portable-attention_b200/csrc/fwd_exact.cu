@@ -2,7 +2,8 @@
 // masks, grouped-query heads; fp64 math for fp64 operands, fp32 math (FFMA,
 // no TF32) for fp32/fp16/bf16 operands.
 //
-// One warp owns one query row. Keys stream in chunks of 32 (one key per
+// One warp owns one query row (16 rows per CTA share 32-key K/V tiles in
+// shared memory when E, Ev <= 256). Keys stream in chunks of 32 (one key per
 // lane): the lane forms its score, the warp reduces the chunk max and sum,
 // and the running output row (lanes own value columns) is rescaled and
 // accumulated -- an online softmax whose result equals the two-pass
@@ -144,11 +145,170 @@ __global__ void __launch_bounds__(kWarps * 32) sdpa_exact_kernel(ExactArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tiled variant for E, Ev <= 256: a CTA of 16 warps owns 16 consecutive query
+// rows of one slice (one row per warp, as above) and streams 32-key K and V
+// tiles through shared memory, so each key and value row is read from memory
+// once per 16 query rows instead of once per row. K rows are padded by four
+// elements so that lane j's 16-byte loads of key row j hit distinct banks; q
+// rows sit in shared memory and are read as broadcasts.
+constexpr int kTRows = 16;   // query rows (warps) per CTA
+constexpr int kTKeys = 32;   // keys per tile
+constexpr int kTMaxDim = 256;
+
+__host__ __device__ constexpr int tiled_pitch(int e) { return ((e + 3) & ~3) + 4; }
+
+template <typename Acc>
+__host__ __device__ constexpr size_t tiled_smem(int e, int ev) {
+  return static_cast<size_t>(kTKeys * tiled_pitch(e) + kTKeys * ev + kTRows * tiled_pitch(e)) * sizeof(Acc);
+}
+
+template <typename T, typename Acc, int MASK, typename MaskT, int NC>
+__global__ void __launch_bounds__(kTRows * 32) sdpa_exact_tiled_kernel(ExactArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_t[];
+  const int E = static_cast<int>(a.E), Ev = static_cast<int>(a.Ev);
+  const int KP = tiled_pitch(E);
+  Acc* sK = reinterpret_cast<Acc*>(smem_t);   // [kTKeys][KP]
+  Acc* sV = sK + kTKeys * KP;                  // [kTKeys][Ev]
+  Acc* sQ = sV + kTKeys * Ev;                  // [kTRows][KP]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t groups = (a.L + kTRows - 1) / kTRows;
+  const int64_t slice = blockIdx.x / groups;
+  const int64_t i0 = (blockIdx.x % groups) * kTRows;
+  const int64_t i = i0 + warp;
+  const bool row_live = i < a.L;
+  const SliceOffsets off = slice_offsets(a.lt, slice);
+  const T* qb = static_cast<const T*>(a.q) + off.q;
+  const T* kb = static_cast<const T*>(a.k) + off.k;
+  const T* vb = static_cast<const T*>(a.v) + off.v;
+  const Acc scale = static_cast<Acc>(a.scale);
+  const Acc neg_inf = -static_cast<Acc>(INFINITY);
+
+  {  // warp w stages query row i0 + w (zero-padded to KP columns)
+    const T* src = qb + (i0 + warp) * a.q_rs;
+    for (int e = lane; e < KP; e += 32)
+      sQ[warp * KP + e] = (e < E && i0 + warp < a.L) ? load_as<Acc>(src + e) : Acc(0);
+  }
+  const int64_t s_end = a.causal ? (i + 1 < a.S ? i + 1 : a.S) : a.S;
+  const int64_t last_row = (i0 + kTRows < a.L ? i0 + kTRows : a.L) - 1;
+  const int64_t cta_end = a.causal ? (last_row + 1 < a.S ? last_row + 1 : a.S) : a.S;
+
+  Acc acc[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) acc[c] = 0;
+  Acc m = neg_inf, l = 0;
+  const Acc* qr = sQ + warp * KP;
+
+  for (int64_t j0 = 0; j0 < cta_end; j0 += kTKeys) {
+    __syncthreads();  // the previous tile is consumed (and, first time, sQ is written)
+    // warp w stages key/value rows 2w and 2w + 1 of the tile (lanes over columns)
+#pragma unroll
+    for (int h = 0; h < kTKeys / kTRows; ++h) {
+      const int t = warp * (kTKeys / kTRows) + h;
+      const int64_t key = j0 + t;
+      const bool in = key < a.S;
+      const T* kr = kb + (in ? key : 0) * a.k_rs;
+      const T* vr = vb + (in ? key : 0) * a.v_rs;
+      for (int e = lane; e < KP; e += 32) sK[t * KP + e] = (in && e < E) ? load_as<Acc>(kr + e) : Acc(0);
+      for (int e = lane; e < Ev; e += 32) sV[t * Ev + e] = in ? load_as<Acc>(vr + e) : Acc(0);
+    }
+    __syncthreads();
+    if (!row_live || j0 >= s_end) continue;
+    const int64_t j = j0 + lane;
+    Acc s = neg_inf;
+    if (j < s_end) {
+      const Acc* kr = sK + lane * KP;
+      Acc d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+      for (int e = 0; e < E; e += 4) {  // E is padded with zeros to a multiple of 4
+        if (sizeof(Acc) == 4) {         // 16-byte loads: lane j's key row hits its own banks
+          const float4 kv = *reinterpret_cast<const float4*>(kr + e);
+          const float4 qv = *reinterpret_cast<const float4*>(qr + e);
+          d0 = fma(static_cast<Acc>(qv.x), static_cast<Acc>(kv.x), d0);
+          d1 = fma(static_cast<Acc>(qv.y), static_cast<Acc>(kv.y), d1);
+          d2 = fma(static_cast<Acc>(qv.z), static_cast<Acc>(kv.z), d2);
+          d3 = fma(static_cast<Acc>(qv.w), static_cast<Acc>(kv.w), d3);
+        } else {
+          d0 = fma(qr[e], kr[e], d0);
+          d1 = fma(qr[e + 1], kr[e + 1], d1);
+          d2 = fma(qr[e + 2], kr[e + 2], d2);
+          d3 = fma(qr[e + 3], kr[e + 3], d3);
+        }
+      }
+      s = ((d0 + d1) + (d2 + d3)) * scale;
+      if (MASK == PA_MASK_BOOL) {
+        const uint8_t keep = static_cast<const uint8_t*>(a.mask)[off.m + i * a.m_rs + j * a.m_cs];
+        if (!keep) s = neg_inf;
+      } else if (MASK == PA_MASK_ADD) {
+        s += load_as<Acc>(static_cast<const MaskT*>(a.mask) + off.m + i * a.m_rs + j * a.m_cs);
+      }
+    }
+    const Acc m_new = fmax(m, warp_max(s));
+    if (m_new == neg_inf) continue;  // every key so far masked: nothing accumulates
+    const Acc alpha = (m == neg_inf) ? Acc(0) : exp_acc(m - m_new);
+    const Acc p = (s == neg_inf) ? Acc(0) : exp_acc(s - m_new);
+    l = l * alpha + warp_sum(p);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) acc[c] *= alpha;
+    const int nk = static_cast<int>(s_end - j0 < kTKeys ? s_end - j0 : kTKeys);
+    for (int t = 0; t < nk; ++t) {
+      const Acc pt = __shfl_sync(0xffffffffu, p, t);
+      const Acc* vr = sV + t * Ev;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const int col = lane + 32 * c;
+        if (col < Ev) acc[c] = fma(pt, vr[col], acc[c]);
+      }
+    }
+    m = m_new;
+  }
+  if (!row_live) return;
+  T* orow = static_cast<T*>(a.out) + (slice * a.L + i) * a.Ev;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = lane + 32 * c;
+    if (col < Ev) orow[col] = from_acc<T>(l > 0 ? static_cast<double>(acc[c] / l) : 0.0);
+  }
+  if (a.lse && lane == 0) a.lse[slice * a.L + i] = l > 0 ? static_cast<float>(m + log_acc(l)) : -INFINITY;
+}
+
+template <typename T, typename Acc, int MASK, typename MaskT, int NC>
+pa_status launch_tiled_nc(const ExactArgs& a, cudaStream_t st) {
+  auto kern = sdpa_exact_tiled_kernel<T, Acc, MASK, MaskT, NC>;
+  static uint64_t attr_set = 0;
+  PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), static_cast<int>(tiled_smem<Acc>(kTMaxDim, kTMaxDim)),
+                            &attr_set));
+  const int64_t blocks = a.nslices * ((a.L + kTRows - 1) / kTRows);
+  if (blocks > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "problem too large for the exact kernel");
+  const size_t smem = tiled_smem<Acc>(static_cast<int>(a.E), static_cast<int>(a.Ev));
+  kern<<<static_cast<unsigned>(blocks), kTRows * 32, smem, st>>>(a);
+  PA_CUDA(cudaGetLastError());
+  return PA_OK;
+}
+
+// NC value columns per lane: Ev <= 64, <= 128 or <= 256.
+template <typename T, typename Acc, int MASK, typename MaskT>
+pa_status launch_tiled(const ExactArgs& a, cudaStream_t st) {
+  if (a.Ev <= 64) return launch_tiled_nc<T, Acc, MASK, MaskT, 2>(a, st);
+  if (a.Ev <= 128) return launch_tiled_nc<T, Acc, MASK, MaskT, 4>(a, st);
+  return launch_tiled_nc<T, Acc, MASK, MaskT, 8>(a, st);
+}
+
 template <typename T, typename Acc>
 pa_status launch_typed(const ExactArgs& a, const pa_sdpa_desc& d, cudaStream_t st) {
   const int64_t blocks = a.nslices * ((a.L + kWarps - 1) / kWarps);
   if (blocks > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "problem too large for the exact kernel");
   dim3 grid(static_cast<unsigned>(blocks)), block(kWarps * 32);
+  if (a.E <= kTMaxDim && a.Ev <= kTMaxDim && a.L > 0) {
+    if (d.mask_kind == PA_MASK_NONE || d.is_causal) return launch_tiled<T, Acc, PA_MASK_NONE, float>(a, st);
+    if (d.mask_kind == PA_MASK_BOOL) return launch_tiled<T, Acc, PA_MASK_BOOL, uint8_t>(a, st);
+    switch (d.mask_dtype) {
+      case PA_F16: return launch_tiled<T, Acc, PA_MASK_ADD, __half>(a, st);
+      case PA_BF16: return launch_tiled<T, Acc, PA_MASK_ADD, __nv_bfloat16>(a, st);
+      case PA_F32: return launch_tiled<T, Acc, PA_MASK_ADD, float>(a, st);
+      case PA_F64: return launch_tiled<T, Acc, PA_MASK_ADD, double>(a, st);
+      default: return fail(PA_ERR_INVALID, "unsupported additive mask dtype");
+    }
+  }
   if (d.mask_kind == PA_MASK_NONE || d.is_causal) {
     sdpa_exact_kernel<T, Acc, PA_MASK_NONE, float><<<grid, block, 0, st>>>(a);
   } else if (d.mask_kind == PA_MASK_BOOL) {
