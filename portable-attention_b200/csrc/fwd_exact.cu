@@ -2,8 +2,8 @@
 // masks, grouped-query heads; fp64 math for fp64 operands, fp32 math (FFMA,
 // no TF32) for fp32/fp16/bf16 operands.
 //
-// One warp owns one query row (16 rows per CTA share 32-key K/V tiles in
-// shared memory when E, Ev <= 256). Keys stream in chunks of 32 (one key per
+// One warp owns one query row (when E, Ev <= 256: two rows per warp, 32 rows
+// per CTA sharing 32-key K/V tiles in shared memory). Keys stream in chunks of 32 (one key per
 // lane): the lane forms its score, the warp reduces the chunk max and sum,
 // and the running output row (lanes own value columns) is rescaled and
 // accumulated -- an online softmax whose result equals the two-pass
@@ -152,8 +152,9 @@ __global__ void __launch_bounds__(kWarps * 32) sdpa_exact_kernel(ExactArgs a) {
 // once per 16 query rows instead of once per row. K rows are padded by four
 // elements so that lane j's 16-byte loads of key row j hit distinct banks; q
 // rows sit in shared memory and are read as broadcasts.
-constexpr int kTRows = 16;   // query rows (warps) per CTA
-constexpr int kTKeys = 32;   // keys per tile
+constexpr int kTWarps = 16;             // warps per CTA
+constexpr int kTRows = 2 * kTWarps;     // query rows per CTA: two per warp
+constexpr int kTKeys = 32;              // keys per tile
 constexpr int kTMaxDim = 256;
 
 __host__ __device__ constexpr int tiled_pitch(int e) { return ((e + 3) & ~3) + 4; }
@@ -163,8 +164,23 @@ __host__ __device__ constexpr size_t tiled_smem(int e, int ev) {
   return static_cast<size_t>(kTKeys * tiled_pitch(e) + kTKeys * ev + kTRows * tiled_pitch(e)) * sizeof(Acc);
 }
 
+// Online-softmax step of one row over one tile: returns this lane's p.
+template <typename Acc, int NC>
+__device__ __forceinline__ Acc row_step(Acc s, Acc& m, Acc& l, Acc (&acc)[NC]) {
+  const Acc neg_inf = -static_cast<Acc>(INFINITY);
+  const Acc m_new = fmax(m, warp_max(s));
+  if (m_new == neg_inf) return Acc(0);  // every key so far masked: nothing accumulates
+  const Acc alpha = (m == neg_inf) ? Acc(0) : exp_acc(m - m_new);
+  const Acc p = (s == neg_inf) ? Acc(0) : exp_acc(s - m_new);
+  l = l * alpha + warp_sum(p);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) acc[c] *= alpha;
+  m = m_new;
+  return p;
+}
+
 template <typename T, typename Acc, int MASK, typename MaskT, int NC>
-__global__ void __launch_bounds__(kTRows * 32) sdpa_exact_tiled_kernel(ExactArgs a) {
+__global__ void __launch_bounds__(kTWarps * 32, 2) sdpa_exact_tiled_kernel(ExactArgs a) {
   extern __shared__ __align__(16) uint8_t smem_t[];
   const int E = static_cast<int>(a.E), Ev = static_cast<int>(a.Ev);
   const int KP = tiled_pitch(E);
@@ -175,8 +191,7 @@ __global__ void __launch_bounds__(kTRows * 32) sdpa_exact_tiled_kernel(ExactArgs
   const int64_t groups = (a.L + kTRows - 1) / kTRows;
   const int64_t slice = blockIdx.x / groups;
   const int64_t i0 = (blockIdx.x % groups) * kTRows;
-  const int64_t i = i0 + warp;
-  const bool row_live = i < a.L;
+  const int64_t ia = i0 + 2 * warp, ib = ia + 1;  // this warp's two query rows
   const SliceOffsets off = slice_offsets(a.lt, slice);
   const T* qb = static_cast<const T*>(a.q) + off.q;
   const T* kb = static_cast<const T*>(a.k) + off.k;
@@ -184,27 +199,44 @@ __global__ void __launch_bounds__(kTRows * 32) sdpa_exact_tiled_kernel(ExactArgs
   const Acc scale = static_cast<Acc>(a.scale);
   const Acc neg_inf = -static_cast<Acc>(INFINITY);
 
-  {  // warp w stages query row i0 + w (zero-padded to KP columns)
-    const T* src = qb + (i0 + warp) * a.q_rs;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {  // warp w stages query rows 2w, 2w + 1 (zero-padded to KP)
+    const int64_t r = ia + h;
+    const T* src = qb + r * a.q_rs;
     for (int e = lane; e < KP; e += 32)
-      sQ[warp * KP + e] = (e < E && i0 + warp < a.L) ? load_as<Acc>(src + e) : Acc(0);
+      sQ[(2 * warp + h) * KP + e] = (e < E && r < a.L) ? load_as<Acc>(src + e) : Acc(0);
   }
-  const int64_t s_end = a.causal ? (i + 1 < a.S ? i + 1 : a.S) : a.S;
+  auto row_end = [&](int64_t r) -> int64_t {
+    if (r >= a.L) return 0;
+    return a.causal ? (r + 1 < a.S ? r + 1 : a.S) : a.S;
+  };
+  const int64_t end_a = row_end(ia), end_b = row_end(ib);
+  const int64_t end_w = end_a > end_b ? end_a : end_b;
   const int64_t last_row = (i0 + kTRows < a.L ? i0 + kTRows : a.L) - 1;
   const int64_t cta_end = a.causal ? (last_row + 1 < a.S ? last_row + 1 : a.S) : a.S;
 
-  Acc acc[NC];
+  Acc acc_a[NC], acc_b[NC];
 #pragma unroll
-  for (int c = 0; c < NC; ++c) acc[c] = 0;
-  Acc m = neg_inf, l = 0;
-  const Acc* qr = sQ + warp * KP;
+  for (int c = 0; c < NC; ++c) acc_a[c] = acc_b[c] = 0;
+  Acc m_a = neg_inf, l_a = 0, m_b = neg_inf, l_b = 0;
+  const Acc* qa = sQ + (2 * warp) * KP;
+  const Acc* qbr = qa + KP;
+
+  auto masked = [&](Acc s, int64_t r, int64_t j) -> Acc {
+    if (MASK == PA_MASK_BOOL) {
+      if (!static_cast<const uint8_t*>(a.mask)[off.m + r * a.m_rs + j * a.m_cs]) return neg_inf;
+    } else if (MASK == PA_MASK_ADD) {
+      s += load_as<Acc>(static_cast<const MaskT*>(a.mask) + off.m + r * a.m_rs + j * a.m_cs);
+    }
+    return s;
+  };
 
   for (int64_t j0 = 0; j0 < cta_end; j0 += kTKeys) {
     __syncthreads();  // the previous tile is consumed (and, first time, sQ is written)
     // warp w stages key/value rows 2w and 2w + 1 of the tile (lanes over columns)
 #pragma unroll
-    for (int h = 0; h < kTKeys / kTRows; ++h) {
-      const int t = warp * (kTKeys / kTRows) + h;
+    for (int h = 0; h < kTKeys / kTWarps; ++h) {
+      const int t = warp * (kTKeys / kTWarps) + h;
       const int64_t key = j0 + t;
       const bool in = key < a.S;
       const T* kr = kb + (in ? key : 0) * a.k_rs;
@@ -213,62 +245,68 @@ __global__ void __launch_bounds__(kTRows * 32) sdpa_exact_tiled_kernel(ExactArgs
       for (int e = lane; e < Ev; e += 32) sV[t * Ev + e] = in ? load_as<Acc>(vr + e) : Acc(0);
     }
     __syncthreads();
-    if (!row_live || j0 >= s_end) continue;
+    if (j0 >= end_w) continue;  // warp-uniform: both rows are past their last key
     const int64_t j = j0 + lane;
-    Acc s = neg_inf;
-    if (j < s_end) {
+    Acc sa = neg_inf, sb = neg_inf;
+    if (j < end_w) {
       const Acc* kr = sK + lane * KP;
-      Acc d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+      Acc a0 = 0, a1 = 0, b0 = 0, b1 = 0;
       for (int e = 0; e < E; e += 4) {  // E is padded with zeros to a multiple of 4
         if (sizeof(Acc) == 4) {         // 16-byte loads: lane j's key row hits its own banks
           const float4 kv = *reinterpret_cast<const float4*>(kr + e);
-          const float4 qv = *reinterpret_cast<const float4*>(qr + e);
-          d0 = fma(static_cast<Acc>(qv.x), static_cast<Acc>(kv.x), d0);
-          d1 = fma(static_cast<Acc>(qv.y), static_cast<Acc>(kv.y), d1);
-          d2 = fma(static_cast<Acc>(qv.z), static_cast<Acc>(kv.z), d2);
-          d3 = fma(static_cast<Acc>(qv.w), static_cast<Acc>(kv.w), d3);
+          const float4 xa = *reinterpret_cast<const float4*>(qa + e);
+          const float4 xb = *reinterpret_cast<const float4*>(qbr + e);
+          a0 = fma(static_cast<Acc>(xa.x), static_cast<Acc>(kv.x), a0);
+          a1 = fma(static_cast<Acc>(xa.y), static_cast<Acc>(kv.y), a1);
+          a0 = fma(static_cast<Acc>(xa.z), static_cast<Acc>(kv.z), a0);
+          a1 = fma(static_cast<Acc>(xa.w), static_cast<Acc>(kv.w), a1);
+          b0 = fma(static_cast<Acc>(xb.x), static_cast<Acc>(kv.x), b0);
+          b1 = fma(static_cast<Acc>(xb.y), static_cast<Acc>(kv.y), b1);
+          b0 = fma(static_cast<Acc>(xb.z), static_cast<Acc>(kv.z), b0);
+          b1 = fma(static_cast<Acc>(xb.w), static_cast<Acc>(kv.w), b1);
         } else {
-          d0 = fma(qr[e], kr[e], d0);
-          d1 = fma(qr[e + 1], kr[e + 1], d1);
-          d2 = fma(qr[e + 2], kr[e + 2], d2);
-          d3 = fma(qr[e + 3], kr[e + 3], d3);
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            a0 = fma(qa[e + u], kr[e + u], a0);
+            a1 = fma(qa[e + u + 1], kr[e + u + 1], a1);
+            b0 = fma(qbr[e + u], kr[e + u], b0);
+            b1 = fma(qbr[e + u + 1], kr[e + u + 1], b1);
+          }
         }
       }
-      s = ((d0 + d1) + (d2 + d3)) * scale;
-      if (MASK == PA_MASK_BOOL) {
-        const uint8_t keep = static_cast<const uint8_t*>(a.mask)[off.m + i * a.m_rs + j * a.m_cs];
-        if (!keep) s = neg_inf;
-      } else if (MASK == PA_MASK_ADD) {
-        s += load_as<Acc>(static_cast<const MaskT*>(a.mask) + off.m + i * a.m_rs + j * a.m_cs);
-      }
+      if (j < end_a) sa = masked((a0 + a1) * scale, ia, j);
+      if (j < end_b) sb = masked((b0 + b1) * scale, ib, j);
     }
-    const Acc m_new = fmax(m, warp_max(s));
-    if (m_new == neg_inf) continue;  // every key so far masked: nothing accumulates
-    const Acc alpha = (m == neg_inf) ? Acc(0) : exp_acc(m - m_new);
-    const Acc p = (s == neg_inf) ? Acc(0) : exp_acc(s - m_new);
-    l = l * alpha + warp_sum(p);
-#pragma unroll
-    for (int c = 0; c < NC; ++c) acc[c] *= alpha;
-    const int nk = static_cast<int>(s_end - j0 < kTKeys ? s_end - j0 : kTKeys);
+    const Acc pa = row_step<Acc, NC>(sa, m_a, l_a, acc_a);
+    const Acc pb = row_step<Acc, NC>(sb, m_b, l_b, acc_b);
+    const int nk = static_cast<int>(end_w - j0 < kTKeys ? end_w - j0 : kTKeys);
     for (int t = 0; t < nk; ++t) {
-      const Acc pt = __shfl_sync(0xffffffffu, p, t);
+      const Acc pta = __shfl_sync(0xffffffffu, pa, t);
+      const Acc ptb = __shfl_sync(0xffffffffu, pb, t);
       const Acc* vr = sV + t * Ev;
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
         const int col = lane + 32 * c;
-        if (col < Ev) acc[c] = fma(pt, vr[col], acc[c]);
+        if (col < Ev) {
+          const Acc x = vr[col];
+          acc_a[c] = fma(pta, x, acc_a[c]);
+          acc_b[c] = fma(ptb, x, acc_b[c]);
+        }
       }
     }
-    m = m_new;
   }
-  if (!row_live) return;
-  T* orow = static_cast<T*>(a.out) + (slice * a.L + i) * a.Ev;
+  auto store_row = [&](int64_t r, const Acc (&acc)[NC], Acc m, Acc l) {
+    if (r >= a.L) return;
+    T* orow = static_cast<T*>(a.out) + (slice * a.L + r) * a.Ev;
 #pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int col = lane + 32 * c;
-    if (col < Ev) orow[col] = from_acc<T>(l > 0 ? static_cast<double>(acc[c] / l) : 0.0);
-  }
-  if (a.lse && lane == 0) a.lse[slice * a.L + i] = l > 0 ? static_cast<float>(m + log_acc(l)) : -INFINITY;
+    for (int c = 0; c < NC; ++c) {
+      const int col = lane + 32 * c;
+      if (col < Ev) orow[col] = from_acc<T>(l > 0 ? static_cast<double>(acc[c] / l) : 0.0);
+    }
+    if (a.lse && lane == 0) a.lse[slice * a.L + r] = l > 0 ? static_cast<float>(m + log_acc(l)) : -INFINITY;
+  };
+  store_row(ia, acc_a, m_a, l_a);
+  store_row(ib, acc_b, m_b, l_b);
 }
 
 template <typename T, typename Acc, int MASK, typename MaskT, int NC>
@@ -280,7 +318,7 @@ pa_status launch_tiled_nc(const ExactArgs& a, cudaStream_t st) {
   const int64_t blocks = a.nslices * ((a.L + kTRows - 1) / kTRows);
   if (blocks > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "problem too large for the exact kernel");
   const size_t smem = tiled_smem<Acc>(static_cast<int>(a.E), static_cast<int>(a.Ev));
-  kern<<<static_cast<unsigned>(blocks), kTRows * 32, smem, st>>>(a);
+  kern<<<static_cast<unsigned>(blocks), kTWarps * 32, smem, st>>>(a);
   PA_CUDA(cudaGetLastError());
   return PA_OK;
 }

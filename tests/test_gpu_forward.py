@@ -144,3 +144,17 @@ def test_full_size_workload_rows(cuda_backend, golden_rows, name):
     vmax = np.repeat(vmax, group, axis=1)[:, :, None, :]
     o = out.astype(np.float32)
     assert np.all(o >= vmin - 2e-3) and np.all(o <= vmax + 2e-3)
+
+
+def test_large_call_pipelined_over_batch_chunks_is_bit_identical(cuda_backend):
+    """A call above the pipelining threshold is cut into batch chunks (copy-in, compute
+    and copy-out overlapped on three streams); every row must equal a single launch's."""
+    import pa_b200
+
+    rng = np.random.default_rng(31)
+    q = rng.standard_normal((4, 16, 2048, 128)).astype(np.float16)
+    k = rng.standard_normal((4, 4, 2048, 128)).astype(np.float16)
+    v = rng.standard_normal((4, 4, 2048, 128)).astype(np.float16)
+    got = cuda_backend(q, k, v, is_causal=True, enable_gqa=True)
+    one = pa_b200.sdpa_sharded(q, k, v, is_causal=True, enable_gqa=True, devices=[0])
+    np.testing.assert_array_equal(got, one)
