@@ -184,8 +184,8 @@ pa_status pa_decode_fwd(const pa_sdpa_desc* desc, const void* q, const void* k, 
  *
  * q and out are dense (batch, q_heads, head_dim) in q_dtype; lse (optional)
  * is float32 (batch, q_heads), natural log. Grouped-query attention shares
- * kv head h among q heads [h*G, (h+1)*G), G = q_heads / kv_heads in
- * {1, 2, 4, 8}; head_dim is 64 or 128.
+ * kv head h among q heads [h*G, (h+1)*G), G = q_heads / kv_heads from
+ * 1 to 16; head_dim is 64 or 128.
  *
  * fp8 caches: scores use k * k_scale and the output v * v_scale (per-tensor
  * dequantisation); set both to 1.0 for fp16/bf16 caches. `scale` is the

@@ -78,8 +78,8 @@ struct DecCfg {
   static constexpr int kTileBytes = kTK * kRowBytes;                // 4096: one K (or V) tile
   static_assert(2 * kTileBytes == kStageBytes, "stage = K tile + V tile");
   static constexpr int kRingBytes = kStages * kStageBytes;          // 192 KB
-  static constexpr int kQOff = kRingBytes;                          // G*D floats (G <= 8)
-  static constexpr int kBarOff = kQOff + 8 * D * 4;
+  static constexpr int kQOff = kRingBytes;                          // G*D floats (G <= 16)
+  static constexpr int kBarOff = kQOff + 16 * D * 4;
   static constexpr int kSmemBytes = kBarOff + kStages * 8 + 16 + 1024;
 
   // Byte offset of byte `byte` of key row `row` inside a tile: 64-column
@@ -103,6 +103,7 @@ struct DecArgs {
   int64_t S;                   // bound on every sequence length
   int64_t max_pages;
   int32_t Hq, Hkv, nsplit, chunk;
+  int32_t G;                   // query heads per key/value head (1..16)
   int32_t page_size, piece_rows, num_pages;
   float scale_log2;            // softmax scale * k_scale * log2(e)
 };
@@ -165,7 +166,7 @@ __device__ __forceinline__ uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t s
   return d;
 }
 
-template <int D, int G, bool QBF16, int KV>
+template <int D, int HT, bool QBF16, int KV>
 __global__ void __launch_bounds__(kThreadsDec, 1)
     decode_partial_kernel(const __grid_constant__ CUtensorMap tk,
                           const __grid_constant__ CUtensorMap tv, const DecArgs a) {
@@ -185,6 +186,7 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
   const int64_t pair = blockIdx.x / a.nsplit;  // b * Hkv + kh
   const int64_t b = pair / a.Hkv;
   const int kh = static_cast<int>(pair % a.Hkv);
+  const int G = a.G;  // query heads of this group: rows 0..G-1 of the HT-row head tile
   int64_t len = a.S;
   if (a.seq_lens) {
     len = a.seq_lens[b];
@@ -300,7 +302,10 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
       sl2 = a.scale_log2 * __int_as_float((127 - 14 + e) << 23);
     }
   }
-  uint32_t qa[KS][2];  // A fragments of Q: rows g (a0, a2); rows g + 8 are zero
+  // A fragments of Q: rows g (heads 0-7: a0, a2) and g + 8 (heads 8-15: a1, a3;
+  // zero when the head tile is 8 rows). Rows past the group are zero.
+  constexpr bool kTwo = HT == 16;
+  uint32_t qa[KS][2], qh[KS][2];
 #pragma unroll
   for (int s = 0; s < KS; ++s) {
     const int d0 = kF8 ? (D / 4) * c + 4 * s : 16 * s + 2 * c;
@@ -309,11 +314,21 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
     const float z = g < G ? qs : 0.f;
     qa[s][0] = pack_pair<kMmaBf16>(qr[d0] * z, qr[d0 + 1] * z);
     qa[s][1] = pack_pair<kMmaBf16>(qr[d1] * z, qr[d1 + 1] * z);
+    if (kTwo) {
+      const float* q2 = sq + (g + 8 < G ? g + 8 : 0) * D;
+      const float z2 = g + 8 < G ? qs : 0.f;
+      qh[s][0] = pack_pair<kMmaBf16>(q2[d0] * z2, q2[d0 + 1] * z2);
+      qh[s][1] = pack_pair<kMmaBf16>(q2[d1] * z2, q2[d1 + 1] * z2);
+    }
   }
-  float o[MT][4];
+  auto qa_hi = [&](int s, int w) -> uint32_t { return kTwo ? qh[s][w] : 0u; };
+  float o[MT][4], o2[MT][4];  // O^T for heads 0-7 and (16-row tiles) 8-15
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  for (int mt = 0; mt < MT; ++mt) {
+    o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    o2[mt][0] = o2[mt][1] = o2[mt][2] = o2[mt][3] = 0.f;
+  }
+  float m_run = -INFINITY, l_run = 0.f, m_run2 = -INFINITY, l_run2 = 0.f;
 
   int consumed = 0;
   for (int j = 0; j < n_own; ++j) {
@@ -346,57 +361,74 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
         }
 #pragma unroll
         for (int s = 0; s < KS; ++s)
-          mma16816<kMmaBf16>(sacc[nt], qa[s][0], 0u, qa[s][1], 0u, e4m3x2_to_h2(kw[s]), e4m3x2_to_h2(kw[s] >> 16));
+          mma16816<kMmaBf16>(sacc[nt], qa[s][0], qa_hi(s, 0), qa[s][1], qa_hi(s, 1), e4m3x2_to_h2(kw[s]),
+                             e4m3x2_to_h2(kw[s] >> 16));
       } else {
         const int row = 8 * nt + (lane & 7);
 #pragma unroll
         for (int s2 = 0; s2 < KS / 2; ++s2) {
           uint32_t b0, b1, b2, b3;
           ldsm_x4(kt + C::off(row, (4 * s2 + (lane >> 3)) * 16), b0, b1, b2, b3);
-          mma16816<kMmaBf16>(sacc[nt], qa[2 * s2][0], 0u, qa[2 * s2][1], 0u, b0, b1);
-          mma16816<kMmaBf16>(sacc[nt], qa[2 * s2 + 1][0], 0u, qa[2 * s2 + 1][1], 0u, b2, b3);
+          mma16816<kMmaBf16>(sacc[nt], qa[2 * s2][0], qa_hi(2 * s2, 0), qa[2 * s2][1], qa_hi(2 * s2, 1), b0, b1);
+          mma16816<kMmaBf16>(sacc[nt], qa[2 * s2 + 1][0], qa_hi(2 * s2 + 1, 0), qa[2 * s2 + 1][1],
+                             qa_hi(2 * s2 + 1, 1), b2, b3);
         }
       }
     }
 
-    // ---- online softmax (head g; keys 8 nt + 2c + j)
-    float mx = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float x = (8 * nt + 2 * c + e) < rem ? sacc[nt][e] * sl2 : -INFINITY;
-        sacc[nt][e] = x;
-        mx = fmaxf(mx, x);
-      }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    // ---- online softmax: head g on accumulator columns 0-1, head g + 8 (16-row
+    // head tiles) on columns 2-3; keys 8 nt + 2c + e.
     // The running max moves only when a score exceeds it by more than 2^8
     // (p <= 256 stays exact enough in f16/bf16 and fp32 sums), so after the
-    // first tiles the accumulators are rarely rescaled; mx is finite because
-    // the tile has at least one valid key.
-    const bool moved = mx > m_run + 8.f;
-    const float m_new = moved ? mx : m_run;
-    const float alpha = ex2(m_run - m_new);
-    m_run = m_new;
-    float psum = 0.f;
-    uint32_t pb[PS][2];  // B fragments of P^T for the 16-key steps
+    // first tiles the accumulators are rarely rescaled; the max is finite
+    // because the tile has at least one valid key.
+    auto head_softmax = [&](int e0, float& m_h, float& l_h, uint32_t (&pbh)[PS][2], float& alpha_h) -> bool {
+      float mx = -INFINITY;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const float p0 = ex2(sacc[nt][0] - m_new), p1 = ex2(sacc[nt][1] - m_new);
-      psum += p0 + p1;
-      pb[nt >> 1][nt & 1] = pack_pair<kMmaBf16>(p0, p1);
-    }
-    l_run = l_run * alpha + psum;
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x = (8 * nt + 2 * c + e) < rem ? sacc[nt][e0 + e] * sl2 : -INFINITY;
+          sacc[nt][e0 + e] = x;
+          mx = fmaxf(mx, x);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const bool mv = mx > m_h + 8.f;
+      const float m_new = mv ? mx : m_h;
+      alpha_h = ex2(m_h - m_new);
+      m_h = m_new;
+      float psum = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float p0 = ex2(sacc[nt][e0] - m_new), p1 = ex2(sacc[nt][e0 + 1] - m_new);
+        psum += p0 + p1;
+        pbh[nt >> 1][nt & 1] = pack_pair<kMmaBf16>(p0, p1);
+      }
+      l_h = l_h * alpha_h + psum;
+      return mv;
+    };
+    uint32_t pb[PS][2], pb2[PS][2];  // B fragments of P^T for the 16-key steps
+    float alpha = 1.f, alpha2 = 1.f;
+    bool moved = head_softmax(0, m_run, l_run, pb, alpha);
+    if (kTwo) moved = head_softmax(2, m_run2, l_run2, pb2, alpha2) || moved;
     if (__any_sync(0xffffffffu, moved)) {
       const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * c);      // head 2c
       const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);  // head 2c + 1
+      const float bl0 = __shfl_sync(0xffffffffu, alpha2, 8 * c);     // head 8 + 2c
+      const float bl1 = __shfl_sync(0xffffffffu, alpha2, 8 * c + 4); // head 9 + 2c
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         o[mt][0] *= al0;
         o[mt][1] *= al1;
         o[mt][2] *= al0;
         o[mt][3] *= al1;
+        if (kTwo) {
+          o2[mt][0] *= bl0;
+          o2[mt][1] *= bl1;
+          o2[mt][2] *= bl0;
+          o2[mt][3] *= bl1;
+        }
       }
     }
 
@@ -430,10 +462,16 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
         for (int w = 0; w < W; ++w) {
           const uint32_t x01 = byte_perm(r[0][w], r[1][w], 0x5140), y01 = byte_perm(r[0][w], r[1][w], 0x7362);
           const uint32_t x23 = byte_perm(r[2][w], r[3][w], 0x5140), y23 = byte_perm(r[2][w], r[3][w], 0x7362);
-          mma16816<kMmaBf16>(o[2 * w], e4m3x2_to_h2(x01), e4m3x2_to_h2(x01 >> 16), e4m3x2_to_h2(x23),
-                             e4m3x2_to_h2(x23 >> 16), pb[sp][0], pb[sp][1]);
-          mma16816<kMmaBf16>(o[2 * w + 1], e4m3x2_to_h2(y01), e4m3x2_to_h2(y01 >> 16), e4m3x2_to_h2(y23),
-                             e4m3x2_to_h2(y23 >> 16), pb[sp][0], pb[sp][1]);
+          const uint32_t ax0 = e4m3x2_to_h2(x01), ax1 = e4m3x2_to_h2(x01 >> 16);
+          const uint32_t ax2 = e4m3x2_to_h2(x23), ax3 = e4m3x2_to_h2(x23 >> 16);
+          const uint32_t ay0 = e4m3x2_to_h2(y01), ay1 = e4m3x2_to_h2(y01 >> 16);
+          const uint32_t ay2 = e4m3x2_to_h2(y23), ay3 = e4m3x2_to_h2(y23 >> 16);
+          mma16816<kMmaBf16>(o[2 * w], ax0, ax1, ax2, ax3, pb[sp][0], pb[sp][1]);
+          mma16816<kMmaBf16>(o[2 * w + 1], ay0, ay1, ay2, ay3, pb[sp][0], pb[sp][1]);
+          if (kTwo) {
+            mma16816<kMmaBf16>(o2[2 * w], ax0, ax1, ax2, ax3, pb2[sp][0], pb2[sp][1]);
+            mma16816<kMmaBf16>(o2[2 * w + 1], ay0, ay1, ay2, ay3, pb2[sp][0], pb2[sp][1]);
+          }
         }
       } else {
         const int m = lane >> 3;
@@ -445,7 +483,12 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
         for (int mt = 0; mt < MT; ++mt) {
           uint32_t a0, a1, a2, a3;
           ldsm_x4_t(vt + C::off(row, (2 * mt + (m & 1)) * 16), a0, a1, a2, a3);
-          mma16816<kMmaBf16>(o[mt], a0 & mlo, a1 & mlo, a2 & mhi, a3 & mhi, pb[sp][0], pb[sp][1]);
+          a0 &= mlo;
+          a1 &= mlo;
+          a2 &= mhi;
+          a3 &= mhi;
+          mma16816<kMmaBf16>(o[mt], a0, a1, a2, a3, pb[sp][0], pb[sp][1]);
+          if (kTwo) mma16816<kMmaBf16>(o2[mt], a0, a1, a2, a3, pb2[sp][0], pb2[sp][1]);
         }
       }
     }
@@ -463,9 +506,11 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
       mbar_drain(full + warp + kWarpsC * (j % kDepth), (j / kDepth) & 1);
   __syncwarp();
 
-  // Per-thread sums -> per-head sums (the four threads of head g).
+  // Per-thread sums -> per-head sums (the four threads of head g, and g + 8).
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  l_run2 += __shfl_xor_sync(0xffffffffu, l_run2, 1);
+  l_run2 += __shfl_xor_sync(0xffffffffu, l_run2, 2);
 
   __syncthreads();  // every tile consumed and landed: the ring is free for the merge
   float* mw = reinterpret_cast<float*>(smem);                 // [8][G] m
@@ -475,6 +520,10 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
     mw[warp * G + g] = m_run;
     lw[warp * G + g] = l_run;
   }
+  if (kTwo && c == 0 && g + 8 < G) {
+    mw[warp * G + g + 8] = m_run2;
+    lw[warp * G + g + 8] = l_run2;
+  }
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -482,6 +531,7 @@ __global__ void __launch_bounds__(kThreadsDec, 1)
       const int h = 2 * c + (i & 1), half = i >> 1;
       const int d = kF8 ? (D / 8) * g + 2 * mt + half : 16 * mt + 8 * half + g;
       if (h < G) aw[(warp * G + h) * D + d] = o[mt][i];
+      if (kTwo && h + 8 < G) aw[(warp * G + h + 8) * D + d] = o2[mt][i];
     }
   asm volatile("bar.sync 1, %0;" ::"n"(kWarpsC * 32));
   for (int i = threadIdx.x; i < G * D; i += kWarpsC * 32) {
@@ -579,7 +629,7 @@ pa_status check_shape(DecPlan* p) {
   if (p->D != 64 && p->D != 128) return fail(PA_ERR_UNSUPPORTED, "decode: head dim must be 64 or 128");
   if (p->Hkv < 1 || p->Hq < 1 || p->Hq % p->Hkv) return fail(PA_ERR_INVALID, "decode: q heads must be a multiple of kv heads");
   const int64_t G = p->Hq / p->Hkv;
-  if (G != 1 && G != 2 && G != 4 && G != 8) return fail(PA_ERR_UNSUPPORTED, "decode: group size must be 1, 2, 4 or 8");
+  if (G < 1 || G > 16) return fail(PA_ERR_UNSUPPORTED, "decode: at most 16 query heads per key/value head");
   p->G = static_cast<int>(G);
   if (p->S < 0 || p->S > 0x7fffffffLL - 64) return fail(PA_ERR_UNSUPPORTED, "decode: too many keys");
   return PA_OK;
@@ -675,10 +725,10 @@ size_t plan_ws_bytes(const DecPlan& p) {
   return slots * (p.D + 2) * sizeof(float);
 }
 
-template <int D, int G, bool QBF16, int KV>
+template <int D, int HT, bool QBF16, int KV>
 pa_status launch_dec(const DecPlan& p, const CUtensorMap& tk, const CUtensorMap& tv, DecArgs& a,
                      void* out, float* lse, cudaStream_t st) {
-  auto kern = decode_partial_kernel<D, G, QBF16, KV>;
+  auto kern = decode_partial_kernel<D, HT, QBF16, KV>;
   constexpr int smem = DecCfg<D, KV>::kSmemBytes;
   static uint64_t attr_set = 0;
   PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), smem, &attr_set));
@@ -694,12 +744,9 @@ pa_status launch_dec(const DecPlan& p, const CUtensorMap& tk, const CUtensorMap&
 template <int D, bool QBF16, int KV>
 pa_status launch_dec_g(const DecPlan& p, const CUtensorMap& tk, const CUtensorMap& tv, DecArgs& a,
                        void* out, float* lse, cudaStream_t st) {
-  switch (p.G) {
-    case 1: return launch_dec<D, 1, QBF16, KV>(p, tk, tv, a, out, lse, st);
-    case 2: return launch_dec<D, 2, QBF16, KV>(p, tk, tv, a, out, lse, st);
-    case 4: return launch_dec<D, 4, QBF16, KV>(p, tk, tv, a, out, lse, st);
-    default: return launch_dec<D, 8, QBF16, KV>(p, tk, tv, a, out, lse, st);
-  }
+  // Head tile of 8 rows (groups 1-8) or 16 rows (groups 9-16).
+  if (p.G <= 8) return launch_dec<D, 8, QBF16, KV>(p, tk, tv, a, out, lse, st);
+  return launch_dec<D, 16, QBF16, KV>(p, tk, tv, a, out, lse, st);
 }
 
 template <int D>
@@ -748,6 +795,7 @@ pa_status run_plan(const DecPlan& p, const void* q, const void* k, const void* v
   a.max_pages = p.max_pages;
   a.Hq = static_cast<int32_t>(p.Hq);
   a.Hkv = static_cast<int32_t>(p.Hkv);
+  a.G = p.G;
   a.nsplit = p.nsplit;
   a.chunk = p.chunk;
   a.page_size = static_cast<int32_t>(p.page_size);

@@ -54,11 +54,11 @@ def _arena() -> DeviceArena:
 def use_decode_kernel(plan) -> bool:
     """Length-1 fp16 queries over dense (B, H, S, D) key/value go to split-KV decode.
 
-    The decode kernel serves grouped-query groups of 1, 2, 4 or 8 query heads
-    per key/value head; other groups take the tensor-core forward.
+    The decode kernel serves grouped-query groups of 1 to 16 query heads per
+    key/value head; larger groups take the tensor-core forward.
     """
     d = plan.desc
-    return (plan.group in (1, 2, 4, 8) and plan.L == 1 and plan.cdt == np.float16 and plan.E == plan.Ev and plan.E in (64, 128)
+    return (1 <= plan.group <= 16 and plan.L == 1 and plan.cdt == np.float16 and plan.E == plan.Ev and plan.E in (64, 128)
             and plan.mask_kind == PA_MASK_NONE and not d.is_causal and plan.S >= 1
             and len(plan.out_lead) >= 1 and _dense_decode(plan))
 

@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("hd", [64, 128])
-@pytest.mark.parametrize("hq,hkv", [(8, 8), (8, 4), (8, 2), (16, 2)])
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (8, 4), (8, 2), (16, 2), (6, 2), (12, 2), (18, 2), (32, 2), (5, 5)])
 def test_decode_matches_oracle(cuda_backend, hd, hq, hkv):
     rng = np.random.default_rng(hd * 100 + hq * 10 + hkv)
     for S in (1, 31, 33, 1000, 4099):
@@ -40,7 +40,10 @@ def test_decode_routes_to_decode_kernel():
     assert use_decode_kernel(plan)
     plan = pa_b200.plan_call((2, 6, 1, 128), (2, 2, 100, 128), (2, 2, 100, 128),
                              np.float16, np.float16, np.float16, group=3)
-    assert not use_decode_kernel(plan)  # group of 3 takes the tensor-core forward
+    assert use_decode_kernel(plan)  # any group of 1 to 16 query heads per key/value head
+    plan = pa_b200.plan_call((2, 34, 1, 128), (2, 2, 100, 128), (2, 2, 100, 128),
+                             np.float16, np.float16, np.float16, group=17)
+    assert not use_decode_kernel(plan)  # a group of 17 takes the tensor-core forward
 
 
 def test_decode_explicit_workspace_and_lse():

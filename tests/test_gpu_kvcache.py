@@ -68,7 +68,7 @@ def test_varlen_contiguous_cache(D, hq, hkv):
 
 @pytest.mark.parametrize("page_size,layout,D,hq,hkv", [
     (16, "hnd", 64, 16, 2), (32, "nhd", 128, 4, 4), (8, "hnd", 128, 8, 4), (64, "nhd", 64, 8, 1),
-    (16, "nhd", 128, 32, 8),
+    (16, "nhd", 128, 32, 8), (16, "hnd", 128, 32, 2), (32, "hnd", 64, 12, 1),
 ])
 def test_paged_cache(page_size, layout, D, hq, hkv):
     import pa_b200
@@ -87,7 +87,8 @@ def test_paged_cache(page_size, layout, D, hq, hkv):
     check(out, lse, want, want_lse)
 
 
-@pytest.mark.parametrize("paged,D,hq,hkv", [(True, 128, 32, 8), (False, 64, 16, 2), (True, 64, 8, 8)])
+@pytest.mark.parametrize("paged,D,hq,hkv", [(True, 128, 32, 8), (False, 64, 16, 2), (True, 64, 8, 8),
+                                             (True, 128, 24, 2), (False, 128, 14, 1)])
 def test_fp8_e4m3_cache(paged, D, hq, hkv):
     import pa_b200
 

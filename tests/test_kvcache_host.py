@@ -149,7 +149,7 @@ def test_kv_cache_desc_strides():
     (dict(page_size=12), 2, "multiple of 8"),
     (dict(max_pages_per_seq=3), 1, "cover max_seq_len"),
     (dict(head_dim=96), 2, "64 or 128"),
-    (dict(q_heads=24), 2, "group size"),
+    (dict(q_heads=68), 2, "at most 16"),
     (dict(kv_dtype=2), 2, "query's dtype or fp8"),
     (dict(scale=float("nan")), 1, "finite"),
 ])
