@@ -17,11 +17,14 @@
 //                     S^T / dP^T are double-buffered so the next block's MMAs
 //                     overlap this block's softmax. dK, dV stay in TMEM until
 //                     the end: grouped-query heads are summed in place.
-//   bwd_dq_kernel     CTA = 128 query rows of one (batch, head). Loops over
-//                     64-key blocks:  S = Q K^T, dP = dO V^T (SS),
+//   bwd_dq_kernel     CTA = 128 query rows of one (batch, head). Its Q and
+//                     dO rows are written once into TMEM by the softmax
+//                     warps (thread <-> row), then it loops over 64-key
+//                     blocks:  S = Q K^T, dP = dO V^T (TS: A from TMEM, so
+//                     each MMA reads only K or V from shared memory),
 //                     dS -> fp16 into TMEM, dQ += dS K (TS, B = K MN-major).
 // TMEM (512 columns): dkdv S^T[2] 0..127, dP^T[2] 128..255, dV, dK after;
-// dq S[2] 0..127, dP[2] 128..255, dQ at 256.
+// dq S[2] 0..127, dP[2] 128..255, dQ at 256, Q at 384, dO at 384 + D/2.
 // Masking matches the forward: top-left causal (key j visible to row i iff
 // j <= i), keys >= S and rows >= L contribute nothing, and rows whose lse is
 // -inf (fully masked) have P = 0 and so zero gradient.
@@ -44,6 +47,8 @@ struct BwdArgs {
   void* dk;
   void* dv;
   void* dq;
+  const void* q;       // (slices_q, L, D), read row by row into tensor memory by the dQ kernel
+  const void* dout;    // same layout as q
   const float* lse2;   // [slices_q][Lp], log2 units
   const float* delta;  // [slices_q][Lp]
   int* status;
@@ -394,32 +399,32 @@ template <int D>
 struct DqCfg {
   static constexpr int BQ = 128, BK = 64;
   static constexpr int kBoxes = D / 64;
-  static constexpr int kQBytes = BQ * D * 2;
   static constexpr int kKBytes = BK * D * 2;
-  static constexpr int kStages = 3;
-  static constexpr int kQOff = 0, kDOOff = kQBytes, kStageOff = 2 * kQBytes;
+  static constexpr int kStages = 4;
+  static constexpr int kStageOff = 0;
   static constexpr int kStageBytes = 2 * kKBytes;
   static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
   static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
-  static constexpr uint32_t kColS = 0, kColP = 128, kColQ = 256;
+  // TMEM columns: S and dP (two 64-column buffers each; dS overwrites dP),
+  // the dQ accumulator, then the CTA's Q and dO rows as fp16/bf16 pairs
+  // (D/2 columns each): S = Q K^T and dP = dO V^T take their A operand from
+  // tensor memory, so each MMA reads only its K or V tile from shared memory.
+  static constexpr uint32_t kColS = 0, kColP = 128, kColQ = 256, kColQa = 384, kColDOa = 384 + D / 2;
 };
 
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreadsB, 1)
-    bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
-                  const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+    bwd_dq_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                   const BwdArgs a) {
   using C = DqCfg<D>;
   constexpr int BQ = C::BQ, BK = C::BK;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sQ = smem + C::kQOff;
-  uint8_t* sDO = smem + C::kDOOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-  uint64_t* q_full = bars;
+  uint64_t* qa_ready = bars;  // Q and dO rows are in tensor memory
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + C::kStages;
   uint64_t* sdp_full = kv_empty + C::kStages;
@@ -443,7 +448,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
   auto stage_ptr = [&](int st) { return smem + C::kStageOff + st * C::kStageBytes; };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(qa_ready, kSoftThreadsB);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(kv_full + s, 1);
       mbar_init(kv_empty + s, 1);
@@ -468,11 +473,6 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 
   if (warp == 0) {
     if (lane == 0 && n > 0) {
-      mbar_expect_tx(q_full, 2 * C::kQBytes);
-      for (int bx = 0; bx < C::kBoxes; ++bx) {
-        tma_load_3d(sQ + bx * (BQ * 128), &tq, q_full, bx * 64, static_cast<int32_t>(m0), static_cast<int32_t>(zq));
-        tma_load_3d(sDO + bx * (BQ * 128), &tdo, q_full, bx * 64, static_cast<int32_t>(m0), static_cast<int32_t>(zq));
-      }
       int last[C::kStages];
 #pragma unroll
       for (int s = 0; s < C::kStages; ++s) last[s] = -1;
@@ -488,7 +488,6 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         }
         last[st] = j;
       }
-      mbar_drain(q_full, 0);
 #pragma unroll
       for (int s = 0; s < C::kStages; ++s)
         if (last[s] >= 0) mbar_drain(kv_full + s, (last[s] / C::kStages) & 1);
@@ -498,24 +497,25 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     if (lane == 0 && n > 0) {
       constexpr uint32_t idS = idesc_f16(128, BK, false, false, BF16);
       constexpr uint32_t idQ = idesc_f16(128, D, false, true, BF16);
-      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
-      bool ok = mbar_wait(q_full, 0, a.status, kStatusTimeoutLoad, abort_flag);
+      bool ok = mbar_wait(qa_ready, 0, a.status, kStatusTimeoutSoftmax, abort_flag);
+      if (ok) tc_fence_after();
       auto issue_sdp = [&](int j) -> bool {
         const int st = j % C::kStages;
         if (!mbar_wait(kv_full + st, (j / C::kStages) & 1, a.status, kStatusTimeoutLoad, abort_flag)) return false;
         tc_fence_after();
         const uint32_t sb = j & 1;
         const uint32_t k_addr = smem_u32(stage_ptr(st)), v_addr = k_addr + C::kKBytes;
+        // A = Q (dO) rows from tensor memory: 16 head-dim elements = 8 columns per step.
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t bx = kk / 4, sub = (kk % 4) * 32;
-          umma_ss(tmem + C::kColS + sb * 64, sdesc_sw128(q_addr + bx * (BQ * 128) + sub, 16, 1024),
+          umma_ts(tmem + C::kColS + sb * 64, tmem + C::kColQa + kk * 8,
                   sdesc_sw128(k_addr + bx * (BK * 128) + sub, 16, 1024), idS, kk > 0);
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t bx = kk / 4, sub = (kk % 4) * 32;
-          umma_ss(tmem + C::kColP + sb * 64, sdesc_sw128(do_addr + bx * (BQ * 128) + sub, 16, 1024),
+          umma_ts(tmem + C::kColP + sb * 64, tmem + C::kColDOa + kk * 8,
                   sdesc_sw128(v_addr + bx * (BK * 128) + sub, 16, 1024), idS, kk > 0);
         }
         tc_commit(sdp_full + sb);
@@ -555,6 +555,29 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     const float lz = a.lse2[zq * a.Lp + row];  // padded rows hold -inf
     const float dlt = a.delta[zq * a.Lp + row];
     const bool row_live = row < a.L && lz != -INFINITY;
+    if (n > 0) {
+      // This thread's row of Q (first warpgroup) or dO (second) into its TMEM
+      // lane as the A operand of S = Q K^T or dP = dO V^T; rows past L are zero.
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(half ? a.dout : a.q) +
+                                                        ((zq * a.L + row) * D) * 2);
+      const uint32_t col = half ? C::kColDOa : C::kColQa;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t w[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 x = row < a.L ? src[c * 8 + u] : make_uint4(0u, 0u, 0u, 0u);
+          w[4 * u] = x.x;
+          w[4 * u + 1] = x.y;
+          w[4 * u + 2] = x.z;
+          w[4 * u + 3] = x.w;
+        }
+        tmem_st32(lane_base + col + c * 32, w);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(qa_ready);
+    }
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       const uint32_t sb = j & 1;
@@ -650,13 +673,11 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
     }
     const CUtensorMapDataType tdt = BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint64_t rowb = D * 2;
-    CUtensorMap tq64, tdo64, tk128, tv128, tq128, tdo128, tk64, tv64;
+    CUtensorMap tq64, tdo64, tk128, tv128, tk64, tv64;
     rc = encode_tma_3d(&tq64, tdt, q, D, L, n, rowb, rowb * L, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == PA_OK) rc = encode_tma_3d(&tdo64, tdt, dout, D, L, n, rowb, rowb * L, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == PA_OK) rc = encode_tma_3d(&tk128, tdt, k, D, S, nkv, rowb, rowb * S, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == PA_OK) rc = encode_tma_3d(&tv128, tdt, v, D, S, nkv, rowb, rowb * S, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc == PA_OK) rc = encode_tma_3d(&tq128, tdt, q, D, L, n, rowb, rowb * L, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc == PA_OK) rc = encode_tma_3d(&tdo128, tdt, dout, D, L, n, rowb, rowb * L, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == PA_OK) rc = encode_tma_3d(&tk64, tdt, k, D, S, nkv, rowb, rowb * S, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc == PA_OK) rc = encode_tma_3d(&tv64, tdt, v, D, S, nkv, rowb, rowb * S, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != PA_OK) break;
@@ -664,6 +685,8 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
     a.dk = dk;
     a.dv = dv;
     a.dq = dq;
+    a.q = q;
+    a.dout = dout;
     a.lse2 = lse2;
     a.delta = delta;
     a.status = device_status_word();
@@ -702,7 +725,7 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
       auto kern = bwd_dq_kernel<D, BF16>;
       static uint64_t attr_set = 0;
       if ((rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), C::kSmemBytes, &attr_set)) != PA_OK) break;
-      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tq128, tdo128, tk64, tv64, a);
+      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tk64, tv64, a);
       if (cudaGetLastError() != cudaSuccess) {
         rc = fail(PA_ERR_CUDA, "bwd_dq launch failed");
         break;
