@@ -174,3 +174,32 @@ def test_workspace_size_counts_split_partials():
     n = ctypes.c_size_t(0)
     check(lib().pa_decode_kv_workspace_size(ctypes.byref(d), 1, ctypes.byref(n)))
     assert n.value > 0 and n.value % (2 * 16 * (128 + 2) * 4) == 0
+
+
+def _kv_args():
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((2, 8, 64)).astype(np.float16)
+    k = rng.standard_normal((2, 2, 32, 64)).astype(np.float16)
+    return q, k, k.copy()
+
+
+@pytest.mark.parametrize("change,msg", [
+    (lambda q, k, v: (q.astype(np.float32), k, v, {}), "query must be float16"),
+    (lambda q, k, v: (q[0], k, v, {}), "query must be float16"),
+    (lambda q, k, v: (q, k, v, {"kv_format": "e5m2"}), "kv_format must be"),
+    (lambda q, k, v: (q, k.astype(np.float32), v, {}), "caches must be float16"),
+    (lambda q, k, v: (q, k, v, {"kv_format": "e4m3"}), "caches must be uint8"),
+    (lambda q, k, v: (q, k, v[:, :, :16], {}), "differ in shape"),
+    (lambda q, k, v: (q, k, v, {"block_table": np.zeros((3, 2), np.int32)}), "block_table must be"),
+    (lambda q, k, v: (q, k, v, {"seq_lens": np.array([1, 2, 3])}), "seq_lens must have shape"),
+    (lambda q, k, v: (q, k, v, {"layout": "bhsd"}), "layout must be one of"),
+    (lambda q, k, v: (q[:, :, :32], k, v, {}), "does not match the query's"),
+    (lambda q, k, v: (q[:, :7], k, v, {}), "multiple of kv_heads"),
+])
+def test_decode_kv_cache_rejects_bad_arguments_before_any_device_work(change, msg):
+    """Argument errors are raised by the host layer, before the library is touched."""
+    import pa_b200
+
+    q, k, v, kw = change(*_kv_args())
+    with pytest.raises(ValueError, match=msg):
+        pa_b200.decode_kv_cache(q, k, v, **kw)
