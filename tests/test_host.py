@@ -172,3 +172,24 @@ def test_missing_library_raises_not_falls_back(monkeypatch, tmp_path):
     with pytest.raises(_lib.LibraryError):
         _lib.lib()
     assert not pa_b200.available()
+
+
+def test_backward_argument_errors_on_the_host():
+    """sdpa_backward's scope checks run before any device work (no GPU needed)."""
+    import pa_b200
+
+    z = np.zeros((1, 2, 8, 64), np.float16)
+    with pytest.raises(NotImplementedError, match="head dim 64 or 128"):
+        pa_b200.sdpa_backward(z[..., :32], z[..., :32], z[..., :32], z[..., :32])
+    with pytest.raises(NotImplementedError, match="float16"):
+        pa_b200.sdpa_backward(*(z.astype(np.float32),) * 4)
+    with pytest.raises(NotImplementedError, match="attn_mask"):
+        pa_b200.sdpa_backward(z, z, z, z, attn_mask=np.ones((8, 8), bool))
+    with pytest.raises(NotImplementedError, match="dropout_p"):
+        pa_b200.sdpa_backward(z, z, z, z, dropout_p=0.1)
+    with pytest.raises(NotImplementedError, match="head axis"):
+        pa_b200.sdpa_backward(z[0, 0], z[0, 0], z[0, 0], z[0, 0])
+    with pytest.raises(ValueError, match="dout shape"):
+        pa_b200.sdpa_backward(z, z, z, z[..., :4, :])
+    with pytest.raises(ValueError):
+        pa_b200.sdpa_backward(z, z[..., :32], z, z)  # E mismatch: the reference's validation message
