@@ -45,6 +45,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
@@ -58,6 +59,13 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "SDPA TFLOP/s (fwd, fwd+bwd) at 1/2/4/8 B200; decode HBM GB/s; %peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def clock_log(args, rank: int) -> Path:
+    """CSV file for this rank's nvidia-smi clock samples (``--clock-dir``, else a temp folder)."""
+    out_dir = Path(args.clock_dir) if args.clock_dir else Path(tempfile.gettempdir()) / "pa_b200_bench"
+    out_dir.mkdir(parents=True, exist_ok=True)
+    return out_dir / f"clocks_rank{rank}.csv"
 
 
 def peaks():
@@ -402,9 +410,7 @@ def run_gpu(args):
                     mask_ptr=bufs["mask"].ptr if "mask" in bufs else None, stream=stream,
                     decode=decode)
 
-    out_dir = ROOT / "gpurun_out"
-    out_dir.mkdir(exist_ok=True)
-    clocks = ClockSampler(local, out_dir / f"clocks_rank{rank}.csv").start()
+    clocks = ClockSampler(local, clock_log(args, rank)).start()
     for _ in range(args.warmup):
         step()
     stream.synchronize()
@@ -565,9 +571,7 @@ def run_ring(args, rank, local, world, pg):
                       bufs["dout"].ptr, bufs["lse"].ptr, bufs["dq"].ptr, bufs["dk"].ptr,
                       bufs["dv"].ptr, stream)
 
-    out_dir = ROOT / "gpurun_out"
-    out_dir.mkdir(exist_ok=True)
-    clocks = ClockSampler(local, out_dir / f"clocks_rank{rank}.csv").start()
+    clocks = ClockSampler(local, clock_log(args, rank)).start()
     for _ in range(args.warmup):
         step()
     comm.wait(stream, timeout_ms=300000)
@@ -740,9 +744,7 @@ def run_kvcache(args):
                                  block_table_ptr=None if table is None else table.data_ptr(),
                                  stream=stream, workspace=(ws.ptr, ws_bytes))
 
-    out_dir = ROOT / "gpurun_out"
-    out_dir.mkdir(exist_ok=True)
-    clocks = ClockSampler(local, out_dir / f"clocks_rank{rank}.csv").start()
+    clocks = ClockSampler(local, clock_log(args, rank)).start()
     for _ in range(args.warmup):
         step()
     stream.synchronize()
@@ -839,6 +841,8 @@ def main():
     ap.add_argument("--workload", default="fp16_causal_gqa")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--clock-dir", default=None,
+                    help="folder for the per-rank nvidia-smi clock samples (default: a temp folder)")
     ap.add_argument("--batch", type=int, default=None,
                     help="keep only the first BATCH batch rows of the workload (profiling)")
     ap.add_argument("--heads", type=int, default=None,
