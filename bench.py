@@ -40,6 +40,7 @@ cache, the output copied back.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -62,9 +63,16 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 
 def clock_log(args, rank: int) -> Path:
-    """CSV file for this rank's nvidia-smi clock samples (``--clock-dir``, else a temp folder)."""
-    out_dir = Path(args.clock_dir) if args.clock_dir else Path(tempfile.gettempdir()) / "pa_b200_bench"
-    out_dir.mkdir(parents=True, exist_ok=True)
+    """CSV file for this rank's nvidia-smi clock samples.
+
+    ``--clock-dir`` when given; otherwise a fresh private folder per run and
+    rank (``tempfile.mkdtemp``), so concurrent runs never share a file.
+    """
+    if args.clock_dir:
+        out_dir = Path(args.clock_dir)
+        out_dir.mkdir(parents=True, exist_ok=True)
+    else:
+        out_dir = Path(tempfile.mkdtemp(prefix=f"pa_b200_bench_r{rank}_"))
     return out_dir / f"clocks_rank{rank}.csv"
 
 
@@ -175,6 +183,16 @@ def barrier(pg):
         pg.barrier()
 
 
+def sum_over_ranks(pg, value: float, local: int) -> float:
+    if pg is None:
+        return value
+    import torch
+
+    t = torch.tensor([float(value)], dtype=torch.float64, device=f"cuda:{local}")
+    pg.all_reduce(t, op=pg.ReduceOp.SUM)
+    return float(t.item())
+
+
 def max_over_ranks(pg, value: float, local: int) -> float:
     if pg is None:
         return value
@@ -187,19 +205,33 @@ def max_over_ranks(pg, value: float, local: int) -> float:
 
 # ---------------------------------------------------------------- CPU leg
 
-def cpu_sample(name, budget_s=12.0, x=None):
-    """Time the oracle port of ``fused`` on a bounded sample of the workload.
+def cpu_backends():
+    """The reference's CPU backends: ``(fused, reference, benchmark module, kind)``.
 
-    Returns (rate in the metric's unit, threads, description). Work items run
-    in a thread pool, one per host core, each with BLAS pinned to one thread.
-    Items are whole (batch, head) slices, except for decode (whole batch
-    rows) and the 131072-long causal workload (64-row query blocks against
-    the keys they see, with the causal mask as an explicit boolean slice);
-    the reference has no backward, so that baseline is forward-only.
+    The real package (byte-compiled into ``oracle/_ref`` by
+    ``oracle/build_ref.py``, or ``$PA_REFERENCE_SRC``) when it imports; else the
+    oracle's restatement of the same two algorithms, labelled ``port``.
     """
-    import threadpoolctl
+    from oracle import build_ref
 
-    from oracle.sdpa import fused_sdpa
+    pa = build_ref.import_reference()
+    if pa is not None:
+        from portable_attention import benchmark as bm
+
+        return pa.get_backend("fused"), pa.get_backend("reference"), bm, "reference"
+    from oracle.sdpa import fused_sdpa, reference_sdpa
+
+    return fused_sdpa, reference_sdpa, None, "port"
+
+
+def cpu_jobs(name, x=None):
+    """Work items of the workload for the CPU backends: ``([(args, kwargs, work)], what)``.
+
+    Items are whole (batch, head) slices, except for decode (whole batch rows)
+    and the 131072-long causal workload (64-row query blocks against the keys
+    they see, with the causal mask as an explicit boolean slice); the
+    reference has no backward, so that baseline is forward-only.
+    """
     from pa_b200 import workloads
 
     w = workloads.WORKLOADS[name]
@@ -211,9 +243,9 @@ def cpu_sample(name, budget_s=12.0, x=None):
         q = (gen.standard_normal((1, w.q_shape[1], 1, D)) * 0.5).astype(np.float16)
         kv = [(gen.standard_normal((1, w.kv_shape[1], w.kv_shape[2], D)) * 0.5).astype(np.float16)
               for _ in range(2)]
-        jobs = [((q, kv[0], kv[1], {"enable_gqa": True}), 2 * kv[0].nbytes)] * max(threads, 8)
-        what = "batch rows of q (1,32,1,128) vs k/v (1,8,32768,128)"
-    elif name == "fp16_long_causal":
+        jobs = [((q, kv[0], kv[1]), {"enable_gqa": True}, 2 * kv[0].nbytes)] * max(threads, 8)
+        return jobs, "batch rows of q (1,32,1,128) vs k/v (1,8,32768,128)"
+    if name == "fp16_long_causal":
         if x is None:
             x = workloads.make(name)
         jobs = []
@@ -223,22 +255,36 @@ def cpu_sample(name, budget_s=12.0, x=None):
             rows = np.arange(r0, r0 + 64)
             keys = r0 + 64
             m = np.arange(keys)[None, :] <= rows[:, None]
-            item = (x["q"][0, h, r0:r0 + 64], x["k"][0, h, :keys], x["v"][0, h, :keys],
-                    {"attn_mask": m})
-            jobs.append((item, 4.0 * D * float(np.sum(rows + 1))))
-        what = "64-row query blocks (random heads/offsets) vs their visible keys, forward only"
-    else:
-        if x is None:
-            x = workloads.make(name, batch_rows=slice(0, 1))
-        L, S = w.q_shape[2], w.kv_shape[2]
-        unit = 4.0 * L * S * D * (0.5 if w.is_causal else 1.0)
-        jobs = []
-        for h in range(w.q_shape[1]):
-            kw = {"is_causal": True} if w.is_causal else {}
-            if w.masked:
-                kw["attn_mask"] = x["mask"][0, 0]
-            jobs.append(((x["q"][0, h], x["k"][0, h // group], x["v"][0, h // group], kw), unit))
-        what = "(b,h) slices of the workload"
+            jobs.append(((x["q"][0, h, r0:r0 + 64], x["k"][0, h, :keys], x["v"][0, h, :keys]),
+                         {"attn_mask": m}, 4.0 * D * float(np.sum(rows + 1))))
+        return jobs, "64-row query blocks (random heads/offsets) vs their visible keys, forward only"
+    if x is None:
+        x = workloads.make(name, batch_rows=slice(0, 1))
+    L, S = w.q_shape[2], w.kv_shape[2]
+    unit = 4.0 * L * S * D * (0.5 if w.is_causal else 1.0)
+    jobs = []
+    for h in range(w.q_shape[1]):
+        kw = {"is_causal": True} if w.is_causal else {}
+        if w.masked:
+            kw["attn_mask"] = x["mask"][0, 0]
+        jobs.append(((x["q"][0, h], x["k"][0, h // group], x["v"][0, h // group]), kw, unit))
+    return jobs, "(b,h) slices of the workload"
+
+
+def cpu_sample(name, budget_s=12.0, x=None):
+    """Time the reference's ``fused`` CPU backend on a bounded sample of the workload.
+
+    Returns (rate in the metric's unit, threads, description, kind). Work
+    items run in a thread pool, one per host core (NumPy releases the GIL in
+    its GEMMs), each with BLAS pinned to one thread -- the ``fused`` backend's
+    own policy (``fused.py``: one BLAS thread for the compute region), spread
+    over every core.
+    """
+    import threadpoolctl
+
+    fused, _, _, kind = cpu_backends()
+    jobs, what = cpu_jobs(name, x)
+    threads = os.cpu_count() or 1
     done, work = 0, 0.0
     t0 = time.perf_counter()
     with threadpoolctl.threadpool_limits(limits=1), ThreadPoolExecutor(threads) as ex:
@@ -246,14 +292,56 @@ def cpu_sample(name, budget_s=12.0, x=None):
         while True:
             batch = [jobs[(pos + i) % len(jobs)] for i in range(threads)]
             pos += threads
-            list(ex.map(lambda j: fused_sdpa(j[0][0], j[0][1], j[0][2], **j[0][3]), batch))
+            list(ex.map(lambda j: fused(*j[0], **j[1]), batch))
             done += len(batch)
-            work += sum(j[1] for j in batch)
+            work += sum(j[2] for j in batch)
             if time.perf_counter() - t0 > budget_s or done >= 4 * threads:
                 break
     dt = time.perf_counter() - t0
     rate = work / dt / (1e9 if name == "fp16_decode_gqa" else 1e12)
-    return rate, threads, f"{done} {what}, {dt:.1f}s wall"
+    src = "the reference's fused backend" if kind == "reference" else "oracle port of the fused backend"
+    return rate, threads, f"{done} {what}, {dt:.1f}s wall; {src}", kind
+
+
+def cpu_thread_settings(name, x=None, repeats=3):
+    """One work item through each reference CPU backend, at default BLAS threads and at one.
+
+    The reference's benchmark harness measures exactly these two settings
+    (``benchmark.py:170-188`` ``_limit_threads``, ``:126-149``
+    ``describe_threads``). Each figure is the median of ``repeats`` calls
+    after one warm-up, as the rate of the metric's unit.
+    """
+    import threadpoolctl
+
+    fused, reference, bm, kind = cpu_backends()
+    jobs, what = cpu_jobs(name, x)
+    args, kw, work = jobs[0]
+    unit = 1e9 if name == "fp16_decode_gqa" else 1e12
+
+    def limit(n):
+        if bm is not None:
+            return bm._limit_threads(n)
+        return threadpoolctl.threadpool_limits(limits=n) if n else contextlib.nullcontext()
+
+    out = {"cpu_count": os.cpu_count(), "kind": kind,
+           "item": what.split(" of ")[0] + f" (first item, shapes q {args[0].shape} k {args[1].shape})"}
+    if bm is not None:
+        out["describe_threads"] = bm.describe_threads().summary
+    else:
+        out["describe_threads"] = ", ".join(f"{i.get('internal_api')}={i.get('num_threads')}"
+                                            for i in threadpoolctl.threadpool_info())
+    for bname, fn in (("fused", fused), ("reference", reference)):
+        for label, n in (("default", None), ("1", 1)):
+            with limit(n):
+                fn(*args, **kw)
+                times = []
+                for _ in range(repeats):
+                    t0 = time.perf_counter()
+                    fn(*args, **kw)
+                    times.append(time.perf_counter() - t0)
+            ms = statistics.median(times) * 1e3
+            out[f"{bname}_blas_{label}"] = {"ms": ms, "rate": work / (ms * 1e-3) / unit}
+    return out
 
 
 def run_reference(args):
@@ -265,9 +353,11 @@ def run_reference(args):
     if args.workload in KV_WORKLOADS:
         return run_reference_kv(args)
     w = workloads.WORKLOADS[args.workload]
+    # Each step is a bounded sample, sized so the whole run stays within ~2.5 minutes.
+    budget = max(0.5, min(4.0, 150.0 / (args.warmup + args.steps)))
     rates = []
     for i in range(args.warmup + args.steps):
-        rate, threads, desc = cpu_sample(args.workload, budget_s=4.0)
+        rate, threads, desc, kind = cpu_sample(args.workload, budget_s=budget)
         if i >= args.warmup:
             rates.append(rate)
     value = statistics.median(rates)
@@ -275,11 +365,13 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None,
         "dtype": "f32" if w.dtype == "float16" else w.dtype.replace("float", "f"),
         "data": "synthetic", "config": workload_config(args.workload, args.gpus),
-        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
-                         "sample": desc + " per step; oracle port of the fused backend"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": kind,
+                         "sample": desc + " per step",
+                         "thread_settings": cpu_thread_settings(args.workload)},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -308,17 +400,54 @@ def run_reference_kv(args):
 
 
 def workload_config(name, n, x=None):
+    """The ``config`` of a line: the global workload (``x``: a profiling cut of it)."""
     from pa_b200 import workloads
 
     w = workloads.WORKLOADS[name]
     qs = tuple(x["q"].shape) if x is not None else w.q_shape
     ks = tuple(x["k"].shape) if x is not None else w.kv_shape
+    axis = split_axis(w, n)
     return {"workload": f"{name}: q {qs} k/v {ks} {w.dtype}"
                         f"{' causal' if w.is_causal else ''}{' gqa' if w.enable_gqa else ''}"
                         f"{' key-padding mask' if w.masked else ''}",
-            "global_batch": qs[0] * n, "seq_len": qs[2],
-            "parallelism": f"batch-shard x{n}" if n > 1 else "single",
+            "global_batch": qs[0], "seq_len": qs[2],
+            "parallelism": (f"{axis}-shard x{n}: one global problem split over {n} GPUs, "
+                            "no data-path collective" if n > 1 else "single"),
             "l2": "inputs larger than L2 (no flush)"}
+
+
+def split_axis(w, n):
+    """Axis the global problem is cut along for ``n`` ranks: batch rows, else whole KV-head groups."""
+    if n <= 1 or w.q_shape[0] >= n:
+        return "batch"
+    return "head"
+
+
+def rank_part(x, w, n, rank):
+    """This rank's contiguous part of the global inputs (batch rows, or whole grouped-query groups)."""
+    if n <= 1:
+        return x
+    group = w.q_shape[1] // w.kv_shape[1]
+    if split_axis(w, n) == "batch":
+        b = np.array_split(np.arange(x["q"].shape[0]), n)[rank]
+        sl_q = sl_kv = (slice(int(b[0]), int(b[-1]) + 1),)
+        sl_m = sl_q
+    else:
+        kvh = np.array_split(np.arange(x["k"].shape[1]), n)[rank]
+        sl_kv = (slice(None), slice(int(kvh[0]), int(kvh[-1]) + 1))
+        sl_q = (slice(None), slice(int(kvh[0]) * group, (int(kvh[-1]) + 1) * group))
+        sl_m = None
+    out = {}
+    for key, val in x.items():
+        if key in ("q", "dout"):
+            out[key] = np.ascontiguousarray(val[sl_q])
+        elif key in ("k", "v"):
+            out[key] = np.ascontiguousarray(val[sl_kv])
+        elif key == "mask":
+            out[key] = np.ascontiguousarray(val[sl_m]) if sl_m is not None and val.shape[0] > 1 else val
+        elif key == "keep":
+            out[key] = val[sl_m] if sl_m is not None else val
+    return out
 
 
 # ---------------------------------------------------------------- GPU leg
@@ -366,6 +495,11 @@ def run_gpu(args):
     if w.backward and world > 1:
         return run_ring(args, rank, local, world, pg)
     x = shrink(workloads.make(args.workload), w, args.batch, args.heads)
+    x_global = {key: x[key] for key in ("q", "k", "v")}
+    global_flops = fwd_flops(x, w)
+    global_bytes = float(2 * x["k"].nbytes + 2 * x["q"].nbytes)
+    # N > 1: the one global problem is cut into N parts (strong scaling).
+    x = rank_part(x, w, world, rank)
     mask = x.get("mask")
     plan = pa_b200.plan_call(x["q"].shape, x["k"].shape, x["v"].shape, x["q"].dtype, x["k"].dtype,
                              x["v"].dtype, None if mask is None else mask.shape,
@@ -438,7 +572,7 @@ def run_gpu(args):
     if decode:
         unit = "GB/s"
         work = float(2 * x["k"].nbytes + x["q"].nbytes + out_bytes)
-        value = world * work / (ms * 1e-3) / 1e9
+        value = global_bytes / (ms * 1e-3) / 1e9
         achieved = work / (statistics.mean(per) * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / pk["hbm_gbs"], "traffic": traffic_for(args.workload),
@@ -463,7 +597,7 @@ def run_gpu(args):
     else:
         unit = "TFLOP/s"
         work = fwd_flops(x, w)
-        value = world * work / (ms * 1e-3) / 1e12
+        value = global_flops / (ms * 1e-3) / 1e12
         achieved = work / (statistics.mean(per) * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
@@ -499,9 +633,28 @@ def run_gpu(args):
     e2e_ms_local = (time.perf_counter() - t0) * 1e3 / e2e_steps
     barrier(pg)
     e2e_ms = max_over_ranks(pg, e2e_ms_local, local)
-    e2e_val = world * work / (e2e_ms * 1e-3) / (1e9 if decode else 1e12)
-    h2d = sum(a.nbytes for a in host.values()) + (mask.nbytes if mask is not None else 0)
-    d2h = sum(r.nbytes for r in res)
+    global_work = global_bytes if decode else (3.5 * global_flops if backward else global_flops)
+    e2e_val = global_work / (e2e_ms * 1e-3) / (1e9 if decode else 1e12)
+    h2d = sum_over_ranks(pg, sum(a.nbytes for a in host.values()) + (mask.nbytes if mask is not None else 0), local)
+    d2h = sum_over_ranks(pg, sum(r.nbytes for r in res), local)
+
+    # The same public call on ordinary (pageable) NumPy arrays, as most callers hold them.
+    del res
+    plain = {key: np.ascontiguousarray(x[key]) for key in host}
+
+    def pageable_call():
+        if backward:
+            return pa_b200.sdpa_backward(plain["q"], plain["k"], plain["v"], plain["dout"], **kw)
+        return (pa_b200.scaled_dot_product_attention(plain["q"], plain["k"], plain["v"], **kw),)
+
+    res = pageable_call()
+    pg_steps = max(1, min(args.steps, 5))
+    barrier(pg)
+    t0 = time.perf_counter()
+    for _ in range(pg_steps):
+        res = pageable_call()
+    pg_ms = max_over_ranks(pg, (time.perf_counter() - t0) * 1e3 / pg_steps, local)
+    del res
 
     if rank != 0:
         if pg is not None:
@@ -509,21 +662,26 @@ def run_gpu(args):
         return 0
     line = {
         "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16" if plan.cdt == np.float16 else str(plan.cdt).replace("float", "f"),
-        "data": "synthetic", "config": workload_config(args.workload, world, x),
+        "data": "synthetic", "config": workload_config(args.workload, world, x_global),
         "roofline": roof,
         "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
-                "timing": "host wall clock around the synchronous public call"},
-        "gpu_launches": args.steps * launches,
+                "timing": "host wall clock around the synchronous public call, page-locked inputs",
+                "pageable": {"value": global_work / (pg_ms * 1e-3) / (1e9 if decode else 1e12),
+                             "ms_per_step": pg_ms,
+                             "timing": "the same call on ordinary pageable NumPy arrays"}},
+        "gpu_launches": args.steps * launches * world,
         "clocks": clocks.summary(),
         **extra,
     }
     if world == 1 and not args.no_cpu:
-        rate, threads, desc_s = cpu_sample(args.workload, x=x if w.backward else None)
-        line["cpu_baseline"] = {"value": rate, "unit": unit, "cores": threads, "kind": "port",
-                                "sample": desc_s + "; oracle port of the fused backend"}
+        rate, threads, desc_s, kind = cpu_sample(args.workload, x=x if w.backward else None)
+        line["cpu_baseline"] = {"value": rate, "unit": unit, "cores": threads, "kind": kind,
+                                "sample": desc_s,
+                                "thread_settings": cpu_thread_settings(
+                                    args.workload, x=x if w.backward else None)}
     print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()

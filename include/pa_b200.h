@@ -99,9 +99,22 @@ const char* pa_last_error(void);
 pa_status pa_init(int32_t* ndev);
 pa_status pa_set_device(int32_t dev);
 pa_status pa_get_device(int32_t* dev);
-/* Read and clear the device status word of the current device: 0, or the
- * code of a bounded device-side wait that gave up (implies PA_ERR_TIMEOUT). */
+/* Read and clear the device status words of the current device (the
+ * library's own and the one pa_decode_fwd_static uses when given no status
+ * pointer): 0, or the code of a bounded device-side wait that gave up
+ * (0x101-0x105, PA_ERR_TIMEOUT) or of an input error found on the device
+ * (0x201-0x202, PA_ERR_INVALID). Allocates nothing. */
 pa_status pa_device_status(int32_t* code);
+
+/* Failure-path self-test (no reference counterpart; the reference's analogue
+ * is its bounded fence wait, vkcompute.py:1031-1042). Launches one CTA on
+ * `stream` whose first warp waits on an mbarrier nothing arrives on, with a
+ * time bound of `limit_us` microseconds (1 to 1000000), through the same
+ * bounded-wait routine every pipelined kernel uses; its second warp waits on
+ * another such barrier and leaves through the CTA abort flag. The kernel ends
+ * by itself: pa_device_status() then reports code 0x105 (PA_ERR_TIMEOUT) and
+ * the context stays usable. */
+pa_status pa_selftest_wait_timeout(int32_t limit_us, void* stream);
 
 /* ---- memory and streams ------------------------------------------------ */
 
@@ -239,7 +252,10 @@ pa_status pa_decode_kv_fwd(const pa_kv_cache_desc* desc, const void* q, const vo
  *
  * The first call on each device looks up the array's device address with
  * that device current (cudaGetSymbolAddress); make that first call before
- * any stream capture. The entry point calls no cudaMalloc, cudaFree or other
+ * any stream capture. With CUDA's lazy module loading that first call may
+ * also load the library's device code on that device, which is when the
+ * array's 8 MiB are committed: make it at start-up, before any memory budget
+ * applies. The entry point calls no cudaMalloc, cudaFree or other
  * allocating routine.
  *
  * All calls on a device share the one array and it keeps the last call's
@@ -250,7 +266,10 @@ pa_status pa_decode_kv_fwd(const pa_kv_cache_desc* desc, const void* q, const vo
  *
  * `status` (device pointer, may be NULL) receives a nonzero code if a bounded
  * device-side wait gives up; the caller zeroes it beforehand. With NULL the
- * code goes to a library-internal word that is not reported.
+ * code goes to a word inside the library that pa_device_status() reads and
+ * clears (without allocating), so check pa_device_status() after the stream
+ * has finished: the output of a call whose wait gave up is not valid.
+ * q, k, v and out must not be NULL (PA_ERR_INVALID, nothing launched).
  */
 pa_status pa_decode_fwd_static(const pa_sdpa_desc* desc, const void* q, const void* k,
                                const void* v, void* out, float* lse, int32_t* status,

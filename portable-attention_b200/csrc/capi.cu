@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kernels.h"
 
 namespace pa {
 
@@ -174,11 +175,50 @@ pa_status encode_tma_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* ba
   return PA_OK;
 }
 
+namespace {
+
+// One CTA of two warps. Lane 0 of warp 0 waits on an mbarrier that nothing
+// arrives on, with a time bound of `limit_ns`, and gives up: it writes
+// kStatusTimeoutSelfTest and raises the CTA abort flag. Lane 0 of warp 1
+// waits on a second such barrier with the default bound and must leave
+// through the abort flag, long before that bound. This is the give-up path of
+// every pipelined kernel, run on its own.
+__global__ void __launch_bounds__(64) selftest_wait_kernel(int* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / 32;
+  if ((threadIdx.x & 31) == 0)
+    mbar_wait(&bars[warp], 0, status, kStatusTimeoutSelfTest, &abort_flag,
+              warp == 0 ? limit_ns : kWaitNs);
+  __syncthreads();
+}
+
+}  // namespace
+
 }  // namespace pa
 
 using namespace pa;
 
 extern "C" {
+
+pa_status pa_selftest_wait_timeout(int32_t limit_us, void* stream) {
+  clear_error();
+  if (limit_us < 1 || limit_us > 1000000)
+    return fail(PA_ERR_INVALID, "pa_selftest_wait_timeout: limit_us must be in [1, 1000000]");
+  int* status = device_status_word();
+  if (!status) return fail(PA_ERR_CUDA, "device status word unavailable");
+  selftest_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<uint64_t>(limit_us) * 1000ull);
+  PA_CUDA(cudaGetLastError());
+  return PA_OK;
+}
 
 int32_t pa_version(void) { return 100; }  // 0.1.0
 
@@ -206,11 +246,23 @@ pa_status pa_get_device(int32_t* dev) {
 }
 
 pa_status pa_device_status(int32_t* code) {
-  int* w = device_status_word();
-  if (!w) return fail(PA_ERR_CUDA, "device status word unavailable");
+  // The library's word exists once a kernel on this device has used it; no
+  // kernel can have written it before, so it is not allocated here (callers
+  // of the allocation-free decode may call this without allocating).
+  int* w = nullptr;
+  {
+    const int d = current_device();
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (d >= 0 && d < kMaxDevices) w = g_status_words[d];
+  }
   int v = 0;
-  PA_CUDA(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (v) PA_CUDA(cudaMemset(w, 0, sizeof(int)));
+  if (w) {
+    PA_CUDA(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v) PA_CUDA(cudaMemset(w, 0, sizeof(int)));
+  }
+  int v_static = 0;
+  PA_TRY(take_static_decode_status(&v_static));
+  if (!v) v = v_static;
   if (code) *code = v;
   if (v) {
     char buf[96];

@@ -129,6 +129,7 @@ enum : int {
   kStatusTimeoutMma = 0x102,    // waiting for a tensor-core result
   kStatusTimeoutSoftmax = 0x103,
   kStatusTimeoutFree = 0x104,   // producer waiting for a free stage
+  kStatusTimeoutSelfTest = 0x105,  // pa_selftest_wait_timeout's planted wait
   kStatusBadSeqLen = 0x201,     // a sequence length outside [0, max_seq_len]
   kStatusBadPage = 0x202,       // a block-table entry outside [0, num_pages)
 };
@@ -176,15 +177,16 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase of parity `parity` to complete. On give-up it
 // records `code` in the status word, raises the CTA abort flag and returns
 // false; it also returns false at once when another role already aborted.
+// `limit_ns` shortens the time bound (the self-test kernel uses 1 ms).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag, uint64_t limit_ns = kWaitNs) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (mbar_test(bar, parity)) return true;
     if ((i & 255u) == 255u) {
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitNs) {
+      if (global_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicExch(status, code);
         return false;

@@ -852,6 +852,7 @@ extern "C" pa_status pa_decode_fwd(const pa_sdpa_desc* desc, const void* q, cons
   if (lead_count(d) == 0) return PA_OK;
   size_t need = 0;
   PA_TRY(decode_ws_bytes(d, &need));
+  if (!q || !k || !v || !out) return fail(PA_ERR_INVALID, "decode: null q, k, v or out pointer");
   if (workspace) {
     if (workspace_bytes < need) return fail(PA_ERR_INVALID, "decode: workspace smaller than pa_decode_workspace_size");
     return run_decode(d, q, k, v, out, lse, workspace, workspace_bytes, st);
@@ -915,7 +916,8 @@ namespace {
 
 constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
 static __device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
-// Status word for bounded waits when the caller passes none (write-only here).
+// Status word for bounded waits when the caller passes none; pa_device_status
+// reads and clears it together with the library's own word.
 static __device__ __align__(256) int g_decode_static_status[64];
 
 constexpr int kMaxDev = 64;
@@ -946,6 +948,28 @@ pa_status static_scratch_for_current_device(void** scratch, int** status) {
 }
 
 }  // namespace
+
+pa_status take_static_decode_status(int* code) {
+  *code = 0;
+  int dev = 0;
+  PA_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDev) return PA_OK;
+  {
+    // Nothing to read on a device where the static entry point never ran
+    // (its word was never handed to a kernel).
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_status_addr[dev]) return PA_OK;
+  }
+  int v = 0;
+  PA_CUDA(cudaMemcpyFromSymbol(&v, g_decode_static_status, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    PA_CUDA(cudaMemcpyToSymbol(g_decode_static_status, &zero, sizeof(int)));
+  }
+  *code = v;
+  return PA_OK;
+}
+
 }  // namespace pa
 
 extern "C" pa_status pa_decode_fwd_static(const pa_sdpa_desc* desc, const void* q, const void* k,
@@ -965,6 +989,7 @@ extern "C" pa_status pa_decode_fwd_static(const pa_sdpa_desc* desc, const void* 
              need, kStaticScratchBytes);
     return fail(PA_ERR_UNSUPPORTED, buf);
   }
+  if (!q || !k || !v || !out) return fail(PA_ERR_INVALID, "decode: null q, k, v or out pointer");
   void* scratch = nullptr;
   int* own_status = nullptr;
   PA_TRY(static_scratch_for_current_device(&scratch, &own_status));

@@ -29,4 +29,8 @@ pa_status decode_ws_bytes(const pa_sdpa_desc& d, size_t* bytes);
 pa_status run_decode(const pa_sdpa_desc& d, const void* q, const void* k, const void* v, void* out,
                      float* lse, void* ws, size_t ws_bytes, cudaStream_t st);
 
+// Reads and clears the status word pa_decode_fwd_static uses when its caller
+// passes none (0 on a device where that entry point never ran).
+pa_status take_static_decode_status(int* code);
+
 }  // namespace pa

@@ -111,6 +111,7 @@ SIGNATURES = {
     "pa_set_device": [_I32],
     "pa_get_device": [ctypes.POINTER(_I32)],
     "pa_device_status": [ctypes.POINTER(_I32)],
+    "pa_selftest_wait_timeout": [_I32, _P],
     "pa_malloc": [ctypes.POINTER(_P), ctypes.c_size_t],
     "pa_free": [_P],
     "pa_host_alloc": [ctypes.POINTER(_P), ctypes.c_size_t],

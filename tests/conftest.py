@@ -41,6 +41,18 @@ def golden_rows():
 
 
 @pytest.fixture(scope="session")
+def reference_package():
+    """The real reference package: ``$PA_REFERENCE_SRC``, else ``oracle/_ref``
+    (byte-compiled by ``oracle/build_ref.py``, which ``__graft_entry__.build()`` runs)."""
+    from oracle import build_ref
+
+    pa = build_ref.import_reference()
+    if pa is None:
+        pytest.skip("reference package not built (python oracle/build_ref.py)")
+    return pa
+
+
+@pytest.fixture(scope="session")
 def cuda_backend():
     """The CUDA SdpaBackend; fails (not skips) when the GPU path cannot run."""
     import pa_b200

@@ -37,9 +37,71 @@ def test_conformance_case(idx, cuda_backend, golden_conformance):
     assert ok, detail
 
 
-def test_reference_kit_when_importable(cuda_backend):
-    kit = pytest.importorskip("portable_attention.conformance")
-    kit.assert_conforms(cuda_backend)
+def test_reference_kit_runs_unchanged(cuda_backend, reference_package):
+    """The reference's own kit (conformance.py:318 assert_conforms, :300 check_backend,
+    :141 conformance_cases) on the CUDA backend, registered through register_backend."""
+    pa = reference_package
+    pa.assert_conforms(cuda_backend)
+    results = pa.check_backend(cuda_backend, pa.conformance_cases())
+    assert len(results) == 26 and all(r.passed for r in results)
+    from portable_attention.dispatch import _REGISTRY
+
+    saved = dict(_REGISTRY)
+    try:
+        import pa_b200
+
+        assert pa_b200.register()
+        assert "cuda" in pa.available_backends()
+        pa.assert_conforms(pa.get_backend("cuda"))
+    finally:
+        _REGISTRY.clear()
+        _REGISTRY.update(saved)
+
+
+FP32_CASES = [i for i, c in enumerate(CASES) if np.dtype(c.dtype) == np.float32]
+
+
+def _fp32_strict(got, want, v, what):
+    """north_star's fp32 bound: rtol 1e-5, atol 1e-6 * max|v| (no looser)."""
+    atol = 1e-6 * float(np.max(np.abs(v)))
+    np.testing.assert_allclose(got.astype(np.float64), want.astype(np.float64), rtol=1e-5,
+                               atol=atol, err_msg=what)
+
+
+@pytest.mark.parametrize("idx", FP32_CASES, ids=[CASES[i].name for i in FP32_CASES])
+def test_fp32_conformance_within_1e5(idx, cuda_backend, golden_conformance):
+    case = CASES[idx]
+    q, k, v = case.inputs()
+    got = cuda_backend(q, k, v, **case.kwargs)
+    assert got.dtype == np.float32
+    _fp32_strict(got, golden_conformance[f"{idx}_ref"], v, case.name)
+
+
+def test_fp32_extra_cases_within_1e5(cuda_backend, golden_extra):
+    seen = 0
+    for i, (name, (q, k, v), kw) in enumerate(extra_cases()):
+        if q.dtype != np.float32:
+            continue
+        _fp32_strict(cuda_backend(q, k, v, **kw), golden_extra[f"{i}_ref"], v, name)
+        seen += 1
+    assert seen
+
+
+def test_fp32_workload_rows_within_1e5(cuda_backend, golden_rows):
+    """The fp32 unmasked workload q,k,v (4, 8, 512, 64): golden rows at rtol 1e-5."""
+    from pa_b200 import workloads
+
+    x = workloads.make("fp32_unmasked")
+    out = cuda_backend(x["q"], x["k"], x["v"])
+    seen = 0
+    for key, want in golden_rows.items():
+        parts = key.split("|")
+        if parts[0] != "fp32_unmasked" or parts[1] == "fingerprint":
+            continue
+        b, h, r0, nr = map(int, parts[1:])
+        _fp32_strict(out[b, h, r0:r0 + nr], want, x["v"][b, h], key)
+        seen += 1
+    assert seen
 
 
 def test_extra_cases(cuda_backend, golden_extra):

@@ -128,8 +128,8 @@ def test_register_is_a_noop_without_a_gpu(monkeypatch):
     assert calls == []
 
 
-def test_register_into_the_real_registry_when_present(monkeypatch):
-    pa = pytest.importorskip("portable_attention")
+def test_register_into_the_real_registry_when_present(monkeypatch, reference_package):
+    pa = reference_package
     from portable_attention.dispatch import _REGISTRY
 
     saved = dict(_REGISTRY)
@@ -172,6 +172,25 @@ def test_missing_library_raises_not_falls_back(monkeypatch, tmp_path):
     with pytest.raises(_lib.LibraryError):
         _lib.lib()
     assert not pa_b200.available()
+
+
+def test_decode_null_operands_rejected_before_any_launch():
+    """NULL q/k/v/out fail with PA_ERR_INVALID on the host (both decode entry points)."""
+    plan = pa_b200.plan_call((2, 8, 1, 128), (2, 2, 64, 128), (2, 2, 64, 128),
+                             np.float16, np.float16, np.float16, group=4)
+    h = _lib.lib()
+    rc = h.pa_decode_fwd(ctypes.byref(plan.desc), None, None, None, None, None, None, 0, None)
+    assert rc == _lib.PA_ERR_INVALID
+    assert "null" in h.pa_last_error().decode()
+    rc = h.pa_decode_fwd_static(ctypes.byref(plan.desc), None, None, None, None, None, None, None)
+    assert rc == _lib.PA_ERR_INVALID
+    assert "null" in h.pa_last_error().decode()
+
+
+def test_wait_selftest_rejects_out_of_range_limits():
+    h = _lib.lib()
+    for bad in (0, -5, 1000001):
+        assert h.pa_selftest_wait_timeout(bad, None) == _lib.PA_ERR_INVALID
 
 
 def test_backward_argument_errors_on_the_host():

@@ -4,9 +4,13 @@
 while they run (a fixed memory budget after start-up, device memory owned by
 another runtime, serving loops that must not touch the pool): its split
 scratch is a fixed 8 MiB device array inside the library. Here it must give
-the same output as the allocating ``pa_decode_fwd`` (within the fp16 2e-3
-tolerance used throughout), on two calls in a row with different inputs, and
-must reject a problem whose scratch need exceeds the array.
+the same output as the allocating ``pa_decode_fwd`` and as the float64 oracle
+(within the fp16 2e-3 tolerance used throughout), on two calls in a row with
+different inputs, for head groups that take both head-tile widths (4 and 12,
+16); it must reject a problem whose scratch need exceeds the array, leave a
+clean ``pa_device_status`` (which also reads the library's word that the
+entry point writes when the caller passes no status pointer), and change
+nothing in the device's free memory once warm.
 
 This file is named to be collected last, so a first-failure run has already
 run every other test; it also passes alone in a fresh process.
@@ -54,16 +58,25 @@ def _inputs(seed, b=4, hq=16, hkv=4, s=9000, d=128):
     return q, k, v
 
 
-def test_static_scratch_decode_matches_allocating_decode_twice():
+def _plan(q, k, v):
     import pa_b200
+
+    return pa_b200.plan_call(q.shape, k.shape, v.shape, q.dtype, k.dtype, v.dtype,
+                             group=q.shape[1] // k.shape[1])
+
+
+def _close(got, want):
+    np.testing.assert_allclose(got.astype(np.float64), want.astype(np.float64), rtol=2e-3, atol=2e-3)
+
+
+def test_static_scratch_decode_matches_allocating_decode_twice():
     from pa_b200.device import DeviceBuffer
     from pa_b200._lib import check, lib
 
     status = DeviceBuffer(4)
     for seed, shape in ((1, dict()), (2, dict(b=2, hq=8, hkv=8, s=3001, d=64))):
         q, k, v = _inputs(seed, **shape)
-        plan = pa_b200.plan_call(q.shape, k.shape, v.shape, q.dtype, k.dtype, v.dtype,
-                                 group=q.shape[1] // k.shape[1])
+        plan = _plan(q, k, v)
         want_o, want_l = _run("pa_decode_fwd", plan, (q, k, v),
                               lambda st: (None, 0, st.handle))
         check(lib().pa_memset(status.ptr, 0, 4, None))
@@ -74,9 +87,48 @@ def test_static_scratch_decode_matches_allocating_decode_twice():
         check(lib().pa_memcpy_d2h(code.ctypes.data, status.ptr, 4, None))
         check(lib().pa_stream_sync(None))
         assert code[0] == 0
-        np.testing.assert_allclose(got_o.astype(np.float64), want_o.astype(np.float64),
-                                   rtol=2e-3, atol=2e-3)
+        _close(got_o, want_o)
         np.testing.assert_allclose(got_l, want_l, rtol=2e-3, atol=2e-3)
+
+
+def test_static_scratch_decode_matches_oracle_wide_groups():
+    """Groups 12 and 16 run the 16-row head tile; two calls in a row, no status word."""
+    from oracle.sdpa import reference_sdpa
+
+    for seed, shape in ((3, dict(b=2, hq=24, hkv=2, s=5000)), (4, dict(b=3, hq=32, hkv=2, s=2100))):
+        q, k, v = _inputs(seed, **shape)
+        got, _ = _run("pa_decode_fwd_static", _plan(q, k, v), (q, k, v),
+                      lambda st: (None, st.handle))   # NULL status: pa_device_status checked in _run
+        want = reference_sdpa(q, k, v, enable_gqa=True)
+        _close(got, want)
+        assert np.max(np.abs(got.astype(np.float64) - want.astype(np.float64))) <= 2e-3
+
+
+def test_static_scratch_decode_allocates_nothing_once_warm():
+    import torch
+
+    from pa_b200._lib import check, lib
+    from pa_b200.device import DeviceBuffer, Stream
+
+    q, k, v = _inputs(5, b=2, hq=16, hkv=2, s=4096)
+    plan = _plan(q, k, v)
+    st = Stream()
+    bufs = [DeviceBuffer(x.nbytes) for x in (q, k, v, q)]
+    for b, x in zip(bufs, (q, k, v)):
+        check(lib().pa_memcpy_h2d(b.ptr, x.ctypes.data, x.nbytes, st.handle))
+    st.synchronize()
+
+    def call():
+        check(lib().pa_decode_fwd_static(ctypes.byref(plan.desc), bufs[0].ptr, bufs[1].ptr,
+                                         bufs[2].ptr, bufs[3].ptr, None, None, st.handle))
+        st.synchronize()
+
+    call()                                   # first call: symbol lookup, module load
+    free_before, _ = torch.cuda.mem_get_info(torch.cuda.current_device())
+    for _ in range(3):
+        call()
+    free_after, _ = torch.cuda.mem_get_info(torch.cuda.current_device())
+    assert free_after == free_before
 
 
 def test_static_scratch_rejects_oversized_problem():
