@@ -656,6 +656,10 @@ def run_gpu(args):
     pg_ms = max_over_ranks(pg, (time.perf_counter() - t0) * 1e3 / pg_steps, local)
     del res
 
+    ring = None
+    if world > 1 and not args.no_ring and not backward and not decode:
+        ring = ring_subrecord(rank, local, world, pg)
+
     if rank != 0:
         if pg is not None:
             pg.destroy_process_group()
@@ -676,6 +680,8 @@ def run_gpu(args):
         "clocks": clocks.summary(),
         **extra,
     }
+    if ring is not None:
+        line["ring"] = ring
     if world == 1 and not args.no_cpu:
         rate, threads, desc_s, kind = cpu_sample(args.workload, x=x if w.backward else None)
         line["cpu_baseline"] = {"value": rate, "unit": unit, "cores": threads, "kind": kind,
@@ -686,6 +692,81 @@ def run_gpu(args):
     if pg is not None:
         pg.destroy_process_group()
     return 0
+
+
+def ring_subrecord(rank, local, world, pg, steps=3, warmup=2):
+    """The long-context causal fwd+bwd as a ring over the same ranks (one global problem).
+
+    q, k, v, dO (1, 32, 131072, 128) fp16, N(0, 1) like the long-context
+    workload but drawn on each device (``torch.randn``, seed 4 + rank) since
+    only the timing is used; each rank holds its zig-zag shard. Returns the
+    whole-job TFLOP/s (max-over-ranks step time), the forward / backward
+    split, and the per-phase split of one extra profiled step (CUDA events at
+    the phase boundaries inside ``pa_ring_fwd`` / ``pa_ring_bwd``): repacking
+    copies, attention kernels, fp32 accumulation, compute-stream stalls on
+    NCCL, and NCCL transfer time on the side stream.
+    """
+    import torch
+
+    import pa_b200
+    from pa_b200 import workloads
+    from pa_b200.device import Event, Stream
+    from pa_b200.ring import RingComm
+
+    w = workloads.WORKLOADS["fp16_long_causal"]
+    _, H, L, D = w.q_shape
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(4 + rank)
+    shape = (1, H, L // world, D)
+    t = {key: torch.randn(shape, generator=gen, device=dev, dtype=torch.float16)
+         for key in ("q", "k", "v", "dout")}
+    for key in ("out", "dq", "dk", "dv"):
+        t[key] = torch.empty(shape, device=dev, dtype=torch.float16)
+    lse = torch.empty(shape[:-1], device=dev, dtype=torch.float32)
+    torch.cuda.synchronize(dev)
+    plan = pa_b200.plan_call(shape, shape, shape, np.float16, np.float16, np.float16, is_causal=True)
+    comm = RingComm.from_process_group()
+    stream = Stream()
+    p = {key: val.data_ptr() for key, val in t.items()}
+
+    def step(mid=None):
+        comm.forward(plan, p["q"], p["k"], p["v"], p["out"], lse.data_ptr(), stream)
+        if mid is not None:
+            mid.record(stream)
+        comm.backward(plan, p["q"], p["k"], p["v"], p["out"], p["dout"], lse.data_ptr(), p["dq"],
+                      p["dk"], p["dv"], stream)
+
+    try:
+        for _ in range(warmup):
+            step()
+        comm.wait(stream, timeout_ms=300000)
+        ev = [Event() for _ in range(steps + 1)]
+        mids = [Event() for _ in range(steps)]
+        barrier(pg)
+        ev[0].record(stream)
+        for i in range(steps):
+            step(mids[i])
+            ev[i + 1].record(stream)
+        comm.wait(stream, timeout_ms=300000)
+        ms = max_over_ranks(pg, ev[0].elapsed_ms(ev[-1]) / steps, local)
+        fwd_ms = max_over_ranks(pg, statistics.mean(ev[i].elapsed_ms(mids[i]) for i in range(steps)), local)
+        bwd_ms = max_over_ranks(pg, statistics.mean(mids[i].elapsed_ms(ev[i + 1]) for i in range(steps)), local)
+        barrier(pg)
+        comm.profile_start()
+        step()
+        comm.wait(stream, timeout_ms=300000)
+        phases = comm.profile_read()
+        phases_max = {key: max_over_ranks(pg, val, local) for key, val in phases.items()}
+    finally:
+        comm.close()
+    work = w.flops_fwd + w.flops_bwd
+    return {"workload": "fp16_long_causal fwd+bwd: q,k,v,dO (1, 32, 131072, 128) causal, "
+                        "zig-zag sequence shards, inputs drawn on the device",
+            "value": work / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "steps": steps, "warmup": warmup,
+            "phase_ms_rank0": phases, "phase_ms_max_over_ranks": phases_max,
+            "phase_note": "one extra profiled step; attention + accumulate + repack + wait_nccl "
+                          "is the compute stream's busy time, nccl_transfer overlaps it"}
 
 
 def run_ring(args, rank, local, world, pg):
@@ -749,6 +830,12 @@ def run_ring(args, rank, local, world, pg):
     ms = max_over_ranks(pg, events[0].elapsed_ms(events[-1]) / args.steps, local)
     fwd_ms = max_over_ranks(pg, statistics.mean(events[i].elapsed_ms(mids[i]) for i in range(args.steps)), local)
     bwd_ms = max_over_ranks(pg, statistics.mean(mids[i].elapsed_ms(events[i + 1]) for i in range(args.steps)), local)
+    barrier(pg)
+    comm.profile_start()
+    step()
+    comm.wait(stream, timeout_ms=300000)
+    phases = comm.profile_read()
+    phases_max = {key: max_over_ranks(pg, val, local) for key, val in phases.items()}
     work = w.flops_fwd + w.flops_bwd
     value = work / (ms * 1e-3) / 1e12
     pk, pk_kind = peaks()
@@ -793,6 +880,7 @@ def run_ring(args, rank, local, world, pg):
             # per rank per step: fwd 2 per chunk pair + 6 fills/stores, bwd 6 per pair + 8
             "gpu_launches": args.steps * (8 * (2 * world + 1) + 14), "clocks": summary,
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+            "phase_ms_rank0": phases, "phase_ms_max_over_ranks": phases_max,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -999,6 +1087,8 @@ def main():
     ap.add_argument("--workload", default="fp16_causal_gqa")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-ring", action="store_true",
+                    help="N > 1: skip the ring-attention sub-record of the long-context workload")
     ap.add_argument("--clock-dir", default=None,
                     help="folder for the per-rank nvidia-smi clock samples (default: a temp folder)")
     ap.add_argument("--batch", type=int, default=None,

@@ -340,12 +340,30 @@ pa_status pa_comm_destroy(pa_comm* comm);
  * a dead peer ends in an error instead of a hang. */
 pa_status pa_comm_wait(pa_comm* comm, void* stream, int32_t timeout_ms);
 
+/* Phase timing of the ring calls on `comm` (instrumentation; no reference
+ * counterpart). pa_comm_profile_start clears and enables it: the following
+ * pa_ring_fwd / pa_ring_bwd calls record CUDA events at phase boundaries.
+ * pa_comm_profile_read waits for those events, writes the milliseconds spent
+ * per phase (indexes PA_RING_PHASE_*) and disables it again. */
+enum {
+  PA_RING_PHASE_REPACK = 0,      /* chunk copies, fills, output stores (compute stream) */
+  PA_RING_PHASE_ATTENTION = 1,   /* tensor-core kernels of every chunk pair */
+  PA_RING_PHASE_ACCUMULATE = 2,  /* fp32 log-sum-exp merges / gradient accumulation */
+  PA_RING_PHASE_WAIT = 3,        /* compute stream stalled on a transfer */
+  PA_RING_PHASE_NCCL = 4,        /* side stream busy in NCCL send/recv */
+  PA_RING_PHASES = 5
+};
+pa_status pa_comm_profile_start(pa_comm* comm);
+pa_status pa_comm_profile_read(pa_comm* comm, float ms[PA_RING_PHASES]);
+
 /*
  * Ring (context-parallel) causal attention over `comm`. Each rank holds its
  * zig-zag shard of the sequence: chunks r and 2n-1-r of 2n equal chunks, laid
  * out back to back as (B, H, 2*C, D). K/V shards travel around the ring with
  * NCCL send/recv on a side stream while the local block is computed; partial
- * results merge by log-sum-exp. No reference counterpart (the reference has
+ * results merge by log-sum-exp. The backward sends fp32 dK/dV accumulators
+ * along with their K/V (received while the next step's first chunk pair runs)
+ * and home after the last step. No reference counterpart (the reference has
  * no distributed code); the result equals reference.py:56-163 on the gathered
  * sequence.
  */

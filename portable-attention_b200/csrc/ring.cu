@@ -33,6 +33,14 @@ struct pa_comm {
   int nranks, rank, device;
   cudaStream_t side;
   cudaEvent_t ev[4];
+  // Phase timing (pa_comm_profile_start / _read): events recorded at phase
+  // boundaries on the compute stream (marks[0]) and the side stream (marks[1]);
+  // the time from one mark to the next on a stream belongs to the first mark's
+  // phase. Off unless started; events come from a pool kept for reuse.
+  bool profiling;
+  std::vector<std::pair<int, cudaEvent_t>> marks[2];
+  std::vector<cudaEvent_t> event_pool;
+  size_t pool_used;
 };
 
 namespace pa {
@@ -148,6 +156,26 @@ __global__ void fill_f32_kernel(float* p, float v, int64_t n) {
 
 unsigned blocks_for(int64_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
 
+// Phases of a ring call, for pa_comm_profile_read (PA_RING_PHASE_* in the header).
+enum { kPhCopy = 0, kPhAttn = 1, kPhAccum = 2, kPhWait = 3, kPhNccl = 4, kPhEnd = 5 };
+
+// Records a phase boundary on `st` (0: compute stream, 1: side stream) when
+// profiling is on.
+void mark(pa_comm* c, int which, int phase, cudaStream_t st) {
+  if (!c->profiling) return;
+  if (c->pool_used == c->event_pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) {
+      cudaGetLastError();
+      return;
+    }
+    c->event_pool.push_back(e);
+  }
+  cudaEvent_t e = c->event_pool[c->pool_used++];
+  cudaEventRecord(e, st);
+  c->marks[which].push_back({phase, e});
+}
+
 // Dense (B, H, C, D) descriptor for one chunk pair.
 pa_sdpa_desc chunk_desc(const pa_sdpa_desc& d, int64_t C, int causal) {
   pa_sdpa_desc c = d;
@@ -256,6 +284,7 @@ pa_status pa_comm_destroy(pa_comm* c) {
   if (!c) return PA_OK;
   cudaStreamSynchronize(c->side);
   for (auto& e : c->ev) cudaEventDestroy(e);
+  for (auto& e : c->event_pool) cudaEventDestroy(e);
   cudaStreamDestroy(c->side);
   ncclResult_t r = g_nccl.CommDestroy(c->nccl);
   delete c;
@@ -289,6 +318,37 @@ pa_status pa_comm_wait(pa_comm* c, void* stream, int32_t timeout_ms) {
   }
 }
 
+pa_status pa_comm_profile_start(pa_comm* c) {
+  clear_error();
+  if (!c) return fail(PA_ERR_INVALID, "null communicator");
+  c->marks[0].clear();
+  c->marks[1].clear();
+  c->pool_used = 0;
+  c->profiling = true;
+  return PA_OK;
+}
+
+pa_status pa_comm_profile_read(pa_comm* c, float ms[PA_RING_PHASES]) {
+  clear_error();
+  if (!c || !ms) return fail(PA_ERR_INVALID, "null argument");
+  for (int i = 0; i < PA_RING_PHASES; ++i) ms[i] = 0.f;
+  for (int w = 0; w < 2; ++w) {
+    const auto& m = c->marks[w];
+    if (!m.empty()) PA_CUDA(cudaEventSynchronize(m.back().second));
+    for (size_t i = 0; i + 1 < m.size(); ++i) {
+      if (m[i].first == kPhEnd) continue;
+      float t = 0.f;
+      PA_CUDA(cudaEventElapsedTime(&t, m[i].second, m[i + 1].second));
+      ms[m[i].first] += t;
+    }
+  }
+  c->profiling = false;
+  c->marks[0].clear();
+  c->marks[1].clear();
+  c->pool_used = 0;
+  return PA_OK;
+}
+
 pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, const void* k,
                       const void* v, void* out, float* lse, void* stream) {
   clear_error();
@@ -318,6 +378,7 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
   float* acc_l[2] = {reinterpret_cast<float*>(take(rows * 4)), reinterpret_cast<float*>(take(rows * 4))};
   pa_status rc = PA_OK;
   do {
+    mark(comm, 0, kPhCopy, st);
     for (int w = 0; w < 2 && rc == PA_OK; ++w) {
       rc = chunk_copy(qc[w], q, sh.planes_q, C, D, es, w, st);
       if (rc == PA_OK) rc = chunk_copy(kvbuf[0] + w * kvb, k, sh.planes_kv, C, D, es, w, st);
@@ -334,6 +395,7 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
         // read it (step t-1) and the copies above are done.
         cudaEventRecord(comm->ev[0], st);
         cudaStreamWaitEvent(comm->side, comm->ev[0], 0);
+        mark(comm, 1, kPhNccl, comm->side);
         g_nccl.GroupStart();
         g_nccl.Send(kvbuf[cur], 4 * kvb, ncclUint8, (r + 1) % n, comm->nccl, comm->side);
         g_nccl.Recv(kvbuf[nxt], 4 * kvb, ncclUint8, (r - 1 + n) % n, comm->nccl, comm->side);
@@ -342,6 +404,7 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
           rc = fail_nccl(nr, "ring send/recv");
           break;
         }
+        mark(comm, 1, kPhEnd, comm->side);
         cudaEventRecord(comm->ev[1], comm->side);
       }
       for (int qw = 0; qw < 2 && rc == PA_OK; ++qw) {
@@ -350,9 +413,11 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
           const int kid = chunk_id(n, src, kw);
           if (kid > qid) continue;
           pa_sdpa_desc cd = chunk_desc(d, C, kid == qid);
+          mark(comm, 0, kPhAttn, st);
           rc = launch_fwd_tc(cd, qc[qw], kvbuf[cur] + kw * kvb, kvbuf[cur] + (2 + kw) * kvb, nullptr,
                              part_o, part_lse, st);
           if (rc != PA_OK) break;
+          mark(comm, 0, kPhAccum, st);
           if (bf16)
             ring_merge_kernel<true><<<blocks_for(rows * 32, 256), 256, 0, st>>>(part_o, part_lse, acc_o[qw],
                                                                                 acc_l[qw], rows, static_cast<int>(D));
@@ -361,9 +426,13 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
                                                                                  acc_l[qw], rows, static_cast<int>(D));
         }
       }
-      if (t + 1 < n) cudaStreamWaitEvent(st, comm->ev[1], 0);
+      if (t + 1 < n) {
+        mark(comm, 0, kPhWait, st);
+        cudaStreamWaitEvent(st, comm->ev[1], 0);
+      }
     }
     if (rc != PA_OK) break;
+    mark(comm, 0, kPhCopy, st);
     for (int w = 0; w < 2; ++w) {
       if (bf16)
         ring_store_kernel<true><<<blocks_for(rows * D, 256), 256, 0, st>>>(acc_o[w], out, sh.planes_q, C,
@@ -375,6 +444,7 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
         PA_CUDA(cudaMemcpy2DAsync(lse + w * C, 2 * C * 4, acc_l[w], C * 4, C * 4, sh.planes_q,
                                   cudaMemcpyDeviceToDevice, st));
     }
+    mark(comm, 0, kPhEnd, st);
     if (cudaGetLastError() != cudaSuccess) rc = fail(PA_ERR_CUDA, "ring forward launch failed");
   } while (false);
   scratch_free(ws, st);
@@ -421,6 +491,7 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
   auto dvacc = [&](int b, int w) { return reinterpret_cast<float*>(ring[b] + 4 * kvb) + (2 + w) * kv_elems; };
   pa_status rc = PA_OK;
   do {
+    mark(comm, 0, kPhCopy, st);
     for (int w = 0; w < 2 && rc == PA_OK; ++w) {
       rc = chunk_copy(qc[w], q, sh.planes_q, C, D, es, w, st);
       if (rc == PA_OK) rc = chunk_copy(oc[w], out, sh.planes_q, C, D, es, w, st);
@@ -434,13 +505,35 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
     }
     if (rc != PA_OK) break;
     PA_CUDA(cudaMemsetAsync(ring[0] + 4 * kvb, 0, 4 * sh.kv_chunk * 4, st));
+    // Side-stream order per step t (every rank the same, so the point-to-point
+    // operations between neighbours match in order): receive the travelling
+    // dK/dV of the block held in step t (sent by r-1 after its step t-1), send /
+    // receive K/V for step t+1, then, after this step's compute, send the dK/dV
+    // on to r+1 (the last step's send is the hop home). The compute stream waits
+    // for the incoming dK/dV only before its first accumulation into them, so
+    // the transfer overlaps the first chunk pair's backward.
     for (int t = 0; t < n && rc == PA_OK; ++t) {
       const int src = ((r - t) % n + n) % n;
       const int cur = t & 1, nxt = cur ^ 1;
+      if (t > 0) {
+        // ring[cur]'s accumulators were last sent at the end of step t-2, earlier on
+        // this same side stream, so they are free to be overwritten here.
+        mark(comm, 1, kPhNccl, comm->side);
+        ncclResult_t nr = g_nccl.Recv(ring[cur] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8,
+                                      (r - 1 + n) % n, comm->nccl, comm->side);
+        if (nr != ncclSuccess) {
+          rc = fail_nccl(nr, "ring dK/dV recv");
+          break;
+        }
+        mark(comm, 1, kPhEnd, comm->side);
+        cudaEventRecord(comm->ev[1], comm->side);
+      }
       if (t + 1 < n) {
-        // K/V for the next step overlap this step's compute.
+        // K/V for the next step overlap this step's compute; ring[nxt] was last
+        // read by the compute of step t-1.
         cudaEventRecord(comm->ev[0], st);
         cudaStreamWaitEvent(comm->side, comm->ev[0], 0);
+        mark(comm, 1, kPhNccl, comm->side);
         g_nccl.GroupStart();
         g_nccl.Send(ring[cur], 4 * kvb, ncclUint8, (r + 1) % n, comm->nccl, comm->side);
         g_nccl.Recv(ring[nxt], 4 * kvb, ncclUint8, (r - 1 + n) % n, comm->nccl, comm->side);
@@ -449,16 +542,26 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
           rc = fail_nccl(nr, "ring K/V send/recv");
           break;
         }
+        mark(comm, 1, kPhEnd, comm->side);
+        cudaEventRecord(comm->ev[3], comm->side);
       }
+      bool have_acc = t == 0;
       for (int qw = 0; qw < 2 && rc == PA_OK; ++qw) {
         const int qid = chunk_id(n, r, qw);
         for (int kw = 0; kw < 2 && rc == PA_OK; ++kw) {
           const int kid = chunk_id(n, src, kw);
           if (kid > qid) continue;
           pa_sdpa_desc cd = chunk_desc(d, C, kid == qid);
+          mark(comm, 0, kPhAttn, st);
           rc = pa_sdpa_bwd(&cd, qc[qw], kptr(cur, kw), vptr(cur, kw), oc[qw], doc[qw], lc[qw], pdq, pdk,
                            pdv, st);
           if (rc != PA_OK) break;
+          if (!have_acc) {
+            mark(comm, 0, kPhWait, st);
+            cudaStreamWaitEvent(st, comm->ev[1], 0);
+            have_acc = true;
+          }
+          mark(comm, 0, kPhAccum, st);
           const unsigned gq = blocks_for(rows * D, 256), gk = blocks_for(kv_elems, 256);
           if (bf16) {
             add_to_f32_kernel<true><<<gq, 256, 0, st>>>(pdq, dq_acc[qw], rows * D);
@@ -472,24 +575,46 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
         }
       }
       if (rc != PA_OK) break;
-      // dK/dV of the held K/V go to the next rank (after this step's compute);
-      // on the last step this is the hop home.
-      cudaEventRecord(comm->ev[2], st);
-      cudaStreamWaitEvent(comm->side, comm->ev[2], 0);
-      g_nccl.GroupStart();
-      g_nccl.Send(ring[cur] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8, (r + 1) % n, comm->nccl, comm->side);
-      g_nccl.Recv(ring[nxt] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8, (r - 1 + n) % n, comm->nccl, comm->side);
-      ncclResult_t nr = g_nccl.GroupEnd();
-      if (nr != ncclSuccess) {
-        rc = fail_nccl(nr, "ring dK/dV send/recv");
-        break;
+      if (!have_acc) {
+        mark(comm, 0, kPhWait, st);
+        cudaStreamWaitEvent(st, comm->ev[1], 0);
       }
-      cudaEventRecord(comm->ev[3], comm->side);
-      cudaStreamWaitEvent(st, comm->ev[3], 0);
+      if (n > 1) {
+        cudaEventRecord(comm->ev[2], st);
+        cudaStreamWaitEvent(comm->side, comm->ev[2], 0);
+        mark(comm, 1, kPhNccl, comm->side);
+        ncclResult_t nr = g_nccl.Send(ring[cur] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8, (r + 1) % n,
+                                      comm->nccl, comm->side);
+        if (nr != ncclSuccess) {
+          rc = fail_nccl(nr, "ring dK/dV send");
+          break;
+        }
+        mark(comm, 1, kPhEnd, comm->side);
+      }
+      if (t + 1 < n) {
+        mark(comm, 0, kPhWait, st);
+        cudaStreamWaitEvent(st, comm->ev[3], 0);
+      }
     }
     if (rc != PA_OK) break;
-    // After n hops the accumulators of this rank's own K/V sit in ring[n & 1].
-    const int home = n & 1;
+    // This rank's own K/V accumulators come home from r-1 after its last step
+    // (into ring[n & 1], last sent from at the end of step n-2). With one rank
+    // they never left ring[0].
+    const int home = n > 1 ? (n & 1) : 0;
+    if (n > 1) {
+      mark(comm, 1, kPhNccl, comm->side);
+      ncclResult_t nr = g_nccl.Recv(ring[home] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8,
+                                    (r - 1 + n) % n, comm->nccl, comm->side);
+      if (nr != ncclSuccess) {
+        rc = fail_nccl(nr, "ring dK/dV recv (home)");
+        break;
+      }
+      mark(comm, 1, kPhEnd, comm->side);
+      cudaEventRecord(comm->ev[1], comm->side);
+      mark(comm, 0, kPhWait, st);
+      cudaStreamWaitEvent(st, comm->ev[1], 0);
+    }
+    mark(comm, 0, kPhCopy, st);
     for (int w = 0; w < 2; ++w) {
       if (bf16) {
         ring_store_kernel<true><<<blocks_for(rows * D, 256), 256, 0, st>>>(dq_acc[w], dq, sh.planes_q, C,
@@ -507,6 +632,7 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
                                                                            static_cast<int>(D), 2 * C, w * C);
       }
     }
+    mark(comm, 0, kPhEnd, st);
     if (cudaGetLastError() != cudaSuccess) rc = fail(PA_ERR_CUDA, "ring backward launch failed");
   } while (false);
   scratch_free(ws, st);

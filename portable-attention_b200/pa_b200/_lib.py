@@ -141,6 +141,8 @@ SIGNATURES = {
     "pa_comm_init": [ctypes.POINTER(_P), ctypes.c_char_p, _I32, _I32],
     "pa_comm_destroy": [_P],
     "pa_comm_wait": [_P, _P, _I32],
+    "pa_comm_profile_start": [_P],
+    "pa_comm_profile_read": [_P, _P],
     "pa_ring_fwd": [_P, _DESC, _P, _P, _P, _P, _P, _P],
     "pa_ring_bwd": [_P, _DESC, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
 }

@@ -117,6 +117,25 @@ class RingComm:
                                 dout_ptr, lse_ptr, dq_ptr, dk_ptr, dv_ptr,
                                 stream.handle if stream is not None else None))
 
+    PHASES = ("repack", "attention", "accumulate", "wait_nccl", "nccl_transfer")
+
+    def profile_start(self) -> None:
+        """Start timing the phases of the next ring calls (CUDA events at phase boundaries)."""
+        check(lib().pa_comm_profile_start(self.handle))
+
+    def profile_read(self) -> dict:
+        """Milliseconds per phase since :meth:`profile_start` (waits for the recorded events).
+
+        ``repack``: chunk copies, fills and output stores on the compute stream;
+        ``attention``: the tensor-core kernels of every chunk pair;
+        ``accumulate``: fp32 merge / gradient accumulation kernels;
+        ``wait_nccl``: time the compute stream stalled waiting for a transfer;
+        ``nccl_transfer``: time the side stream spent in NCCL send/recv.
+        """
+        ms = (ctypes.c_float * len(self.PHASES))()
+        check(lib().pa_comm_profile_read(self.handle, ms))
+        return dict(zip(self.PHASES, (float(x) for x in ms)))
+
     def close(self) -> None:
         if self.handle:
             check(lib().pa_comm_destroy(self.handle))

@@ -49,10 +49,20 @@ def main():
     for name in ("o", "dq", "dk", "dv"):
         bufs[name] = DeviceBuffer(sq.nbytes)
     bufs["lse"] = DeviceBuffer(B * H * sq.shape[2] * 4)
-    comm.forward(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["o"].ptr, bufs["lse"].ptr, st)
-    comm.backward(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["o"].ptr, bufs["do"].ptr,
-                  bufs["lse"].ptr, bufs["dq"].ptr, bufs["dk"].ptr, bufs["dv"].ptr, st)
-    comm.wait(st, timeout_ms=120000)
+    # Two calls in a row, the second with phase profiling on: the accumulators
+    # and buffers must start clean in every call, and profiling must not change
+    # the results.
+    for it in range(2):
+        if it == 1:
+            comm.profile_start()
+        comm.forward(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["o"].ptr, bufs["lse"].ptr, st)
+        comm.backward(plan, bufs["q"].ptr, bufs["k"].ptr, bufs["v"].ptr, bufs["o"].ptr, bufs["do"].ptr,
+                      bufs["lse"].ptr, bufs["dq"].ptr, bufs["dk"].ptr, bufs["dv"].ptr, st)
+        comm.wait(st, timeout_ms=120000)
+    phases = comm.profile_read()
+    assert phases["attention"] > 0 and all(v >= 0 for v in phases.values()), phases
+    if world > 1:
+        assert phases["nccl_transfer"] > 0, phases
     res = {}
     for name in ("o", "dq", "dk", "dv"):
         res[name] = np.empty_like(sq)
