@@ -658,7 +658,10 @@ def run_gpu(args):
 
     ring = None
     if world > 1 and not args.no_ring and not backward and not decode:
-        ring = ring_subrecord(rank, local, world, pg)
+        try:
+            ring = ring_subrecord(rank, local, world, pg)
+        except Exception as exc:  # noqa: BLE001 -- keep the main line; every rank fails alike
+            ring = {"error": f"{type(exc).__name__}: {exc}"}
 
     if rank != 0:
         if pg is not None:

@@ -209,6 +209,7 @@ struct RingShape {
 
 pa_status ring_shape(const pa_comm* comm, const pa_sdpa_desc& d, RingShape* s) {
   if (!comm) return fail(PA_ERR_INVALID, "ring: null communicator");
+  if (!comm->nccl) return fail(PA_ERR_NCCL, "ring: the communicator was aborted after an error or time-out");
   if (d.dtype != PA_F16 && d.dtype != PA_BF16) return fail(PA_ERR_UNSUPPORTED, "ring: fp16/bf16 only");
   if (!d.is_causal) return fail(PA_ERR_UNSUPPORTED, "ring: causal attention only");
   if (d.L != d.S || d.L % 2) return fail(PA_ERR_INVALID, "ring: local shard must be 2*C rows of q and k");
@@ -286,7 +287,8 @@ pa_status pa_comm_destroy(pa_comm* c) {
   for (auto& e : c->ev) cudaEventDestroy(e);
   for (auto& e : c->event_pool) cudaEventDestroy(e);
   cudaStreamDestroy(c->side);
-  ncclResult_t r = g_nccl.CommDestroy(c->nccl);
+  // An aborted communicator (pa_comm_wait) is already freed.
+  ncclResult_t r = c->nccl ? g_nccl.CommDestroy(c->nccl) : ncclSuccess;
   delete c;
   if (r != ncclSuccess) return fail_nccl(r, "ncclCommDestroy");
   return PA_OK;
@@ -295,6 +297,7 @@ pa_status pa_comm_destroy(pa_comm* c) {
 pa_status pa_comm_wait(pa_comm* c, void* stream, int32_t timeout_ms) {
   clear_error();
   if (!c) return fail(PA_ERR_INVALID, "null communicator");
+  if (!c->nccl) return fail(PA_ERR_NCCL, "the communicator was aborted after an error or time-out");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
@@ -306,12 +309,14 @@ pa_status pa_comm_wait(pa_comm* c, void* stream, int32_t timeout_ms) {
     g_nccl.CommGetAsyncError(c->nccl, &async);
     if (async != ncclSuccess && async != ncclInProgress) {
       g_nccl.CommAbort(c->nccl);
+      c->nccl = nullptr;
       return fail_nccl(async, "NCCL asynchronous error (communicator aborted)");
     }
     const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
                         std::chrono::steady_clock::now() - t0).count();
     if (timeout_ms >= 0 && ms > timeout_ms) {
       g_nccl.CommAbort(c->nccl);
+      c->nccl = nullptr;
       return fail(PA_ERR_TIMEOUT, "ring: peers did not complete in time (communicator aborted)");
     }
     std::this_thread::sleep_for(std::chrono::microseconds(200));
@@ -505,32 +510,22 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
     }
     if (rc != PA_OK) break;
     PA_CUDA(cudaMemsetAsync(ring[0] + 4 * kvb, 0, 4 * sh.kv_chunk * 4, st));
-    // Side-stream order per step t (every rank the same, so the point-to-point
-    // operations between neighbours match in order): receive the travelling
-    // dK/dV of the block held in step t (sent by r-1 after its step t-1), send /
-    // receive K/V for step t+1, then, after this step's compute, send the dK/dV
-    // on to r+1 (the last step's send is the hop home). The compute stream waits
-    // for the incoming dK/dV only before its first accumulation into them, so
-    // the transfer overlaps the first chunk pair's backward.
+    // Side-stream order (every rank the same, so the point-to-point operations
+    // between neighbours match in order): at the start of step t the K/V group
+    // for step t+1 (send to r+1, receive from r-1); after step t's compute the
+    // dK/dV group: send the held block's fp32 accumulators on to r+1 and
+    // receive, from r-1, those of the block held in step t+1 (after the last
+    // step: this rank's own block, home). Each send is grouped with a receive
+    // so every rank's group progresses together: a lone send waits for its
+    // receiver, and a receiver queued behind its own lone send would wait in a
+    // cycle. The compute stream waits for the incoming accumulators only
+    // before its first accumulation into them, so the transfer overlaps the
+    // next step's first chunk-pair backward.
     for (int t = 0; t < n && rc == PA_OK; ++t) {
       const int src = ((r - t) % n + n) % n;
       const int cur = t & 1, nxt = cur ^ 1;
-      if (t > 0) {
-        // ring[cur]'s accumulators were last sent at the end of step t-2, earlier on
-        // this same side stream, so they are free to be overwritten here.
-        mark(comm, 1, kPhNccl, comm->side);
-        ncclResult_t nr = g_nccl.Recv(ring[cur] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8,
-                                      (r - 1 + n) % n, comm->nccl, comm->side);
-        if (nr != ncclSuccess) {
-          rc = fail_nccl(nr, "ring dK/dV recv");
-          break;
-        }
-        mark(comm, 1, kPhEnd, comm->side);
-        cudaEventRecord(comm->ev[1], comm->side);
-      }
       if (t + 1 < n) {
-        // K/V for the next step overlap this step's compute; ring[nxt] was last
-        // read by the compute of step t-1.
+        // ring[nxt]'s K/V were last read by the compute of step t-1.
         cudaEventRecord(comm->ev[0], st);
         cudaStreamWaitEvent(comm->side, comm->ev[0], 0);
         mark(comm, 1, kPhNccl, comm->side);
@@ -545,7 +540,7 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
         mark(comm, 1, kPhEnd, comm->side);
         cudaEventRecord(comm->ev[3], comm->side);
       }
-      bool have_acc = t == 0;
+      bool have_acc = t == 0;  // step 0's accumulators start at zero (memset above)
       for (int qw = 0; qw < 2 && rc == PA_OK; ++qw) {
         const int qid = chunk_id(n, r, qw);
         for (int kw = 0; kw < 2 && rc == PA_OK; ++kw) {
@@ -580,16 +575,23 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
         cudaStreamWaitEvent(st, comm->ev[1], 0);
       }
       if (n > 1) {
+        // ring[nxt]'s accumulators were sent on in step t-1's group, earlier on
+        // this same side stream, so they may be overwritten here.
         cudaEventRecord(comm->ev[2], st);
         cudaStreamWaitEvent(comm->side, comm->ev[2], 0);
         mark(comm, 1, kPhNccl, comm->side);
-        ncclResult_t nr = g_nccl.Send(ring[cur] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8, (r + 1) % n,
-                                      comm->nccl, comm->side);
+        g_nccl.GroupStart();
+        g_nccl.Send(ring[cur] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8, (r + 1) % n, comm->nccl,
+                    comm->side);
+        g_nccl.Recv(ring[nxt] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8, (r - 1 + n) % n, comm->nccl,
+                    comm->side);
+        ncclResult_t nr = g_nccl.GroupEnd();
         if (nr != ncclSuccess) {
-          rc = fail_nccl(nr, "ring dK/dV send");
+          rc = fail_nccl(nr, "ring dK/dV send/recv");
           break;
         }
         mark(comm, 1, kPhEnd, comm->side);
+        cudaEventRecord(comm->ev[1], comm->side);
       }
       if (t + 1 < n) {
         mark(comm, 0, kPhWait, st);
@@ -597,20 +599,10 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
       }
     }
     if (rc != PA_OK) break;
-    // This rank's own K/V accumulators come home from r-1 after its last step
-    // (into ring[n & 1], last sent from at the end of step n-2). With one rank
-    // they never left ring[0].
+    // After the last group this rank's own accumulators sit in ring[n & 1]; with
+    // one rank they never left ring[0].
     const int home = n > 1 ? (n & 1) : 0;
     if (n > 1) {
-      mark(comm, 1, kPhNccl, comm->side);
-      ncclResult_t nr = g_nccl.Recv(ring[home] + 4 * kvb, 4 * sh.kv_chunk * 4, ncclUint8,
-                                    (r - 1 + n) % n, comm->nccl, comm->side);
-      if (nr != ncclSuccess) {
-        rc = fail_nccl(nr, "ring dK/dV recv (home)");
-        break;
-      }
-      mark(comm, 1, kPhEnd, comm->side);
-      cudaEventRecord(comm->ev[1], comm->side);
       mark(comm, 0, kPhWait, st);
       cudaStreamWaitEvent(st, comm->ev[1], 0);
     }
