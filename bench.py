@@ -656,6 +656,13 @@ def run_gpu(args):
     pg_ms = max_over_ranks(pg, (time.perf_counter() - t0) * 1e3 / pg_steps, local)
     del res
 
+    subs = None
+    if args.workload == "fp16_causal_gqa" and not args.no_workloads and args.batch is None and args.heads is None:
+        try:
+            subs = workload_subrecords(rank, local, world, pg)
+        except Exception as exc:  # noqa: BLE001 -- keep the main line; every rank fails alike
+            subs = {"error": f"{type(exc).__name__}: {exc}"}
+
     ring = None
     if world > 1 and not args.no_ring and not backward and not decode:
         try:
@@ -683,6 +690,8 @@ def run_gpu(args):
         "clocks": clocks.summary(),
         **extra,
     }
+    if subs is not None:
+        line["workloads"] = subs
     if ring is not None:
         line["ring"] = ring
     if world == 1 and not args.no_cpu:
@@ -695,6 +704,168 @@ def run_gpu(args):
     if pg is not None:
         pg.destroy_process_group()
     return 0
+
+
+FP32_FFMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # theoretical; no measured fp32 peak exists
+
+
+def _timed(step, steps, warmup, stream, pg, local):
+    """Max-over-ranks mean CUDA-event time of ``step`` (ms), after warm-up."""
+    import pa_b200
+    from pa_b200.device import Event
+
+    for _ in range(warmup):
+        step()
+    stream.synchronize()
+    pa_b200.sync_device_status()
+    ev = [Event() for _ in range(steps + 1)]
+    barrier(pg)
+    ev[0].record(stream)
+    for i in range(steps):
+        step()
+        ev[i + 1].record(stream)
+    stream.synchronize()
+    pa_b200.sync_device_status()
+    return max_over_ranks(pg, ev[0].elapsed_ms(ev[-1]) / steps, local)
+
+
+def workload_subrecords(rank, local, world, pg):
+    """Device-timed lines for the other benchmark configurations, in the same run.
+
+    N = 1: the fp32 exact forward (4, 8, 512, 64), the masked cross-attention
+    forward (16, 16, 1024 x 2048, 64), the split-KV decode (64 x 32 heads,
+    32768 keys) and the long-context causal forward + backward (1, 32,
+    131072, 128). N > 1: the decode with its batch split over the ranks (one
+    global problem, no collective). The two small workloads use their seeded
+    NumPy inputs; the decode and long-context tensors (8 GiB / 4 GiB) are
+    drawn on the device (``torch.randn``, N(0, 1) scaled as the workload
+    says) because only their timing is used.
+    """
+    import ctypes
+
+    import torch
+
+    import pa_b200
+    from pa_b200 import workloads
+    from pa_b200._lib import check, lib
+    from pa_b200.backend import sdpa_device
+    from pa_b200.device import Event, Stream
+
+    pk, pk_kind = peaks()
+    dev = torch.device("cuda", local)
+    stream = Stream()
+    out = {}
+
+    def to_dev(arr):
+        return torch.from_numpy(np.ascontiguousarray(arr)).to(dev)
+
+    if world == 1:
+        for name in ("fp32_unmasked", "fp16_masked_cross"):
+            w = workloads.WORKLOADS[name]
+            x = workloads.make(name)
+            t = {key: to_dev(x[key]) for key in ("q", "k", "v")}
+            m = to_dev(x["mask"].view(np.uint8)) if "mask" in x else None
+            o = torch.empty(w.q_shape[:3] + (w.kv_shape[3],), device=dev, dtype=t["q"].dtype)
+            plan = pa_b200.plan_call(w.q_shape, w.kv_shape, w.kv_shape, x["q"].dtype, x["k"].dtype,
+                                     x["v"].dtype, None if m is None else x["mask"].shape,
+                                     None if m is None else np.bool_, w.is_causal, None, 1)
+            torch.cuda.synchronize(dev)
+
+            def step():
+                sdpa_device(plan, t["q"].data_ptr(), t["k"].data_ptr(), t["v"].data_ptr(),
+                            o.data_ptr(), mask_ptr=None if m is None else m.data_ptr(),
+                            stream=stream, decode=False)
+
+            ms = _timed(step, 50, 5, stream, pg, local)
+            tf = w.flops_fwd / (ms * 1e-3) / 1e12
+            if name == "fp32_unmasked":
+                out[name] = {"value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "kernel": "sdpa_exact_rt (fp32 FFMA)",
+                             "frac_of_fp32_ffma_theoretical": tf / FP32_FFMA_PEAK_TFLOPS,
+                             "peak_note": "148 SMs x 128 FFMA lanes x 2 x 1965 MHz; no measured fp32 peak"}
+            else:
+                out[name] = {"value": tf, "unit": "TFLOP/s", "ms_per_step": ms,
+                             "kernel": "mask_classify + fwd_tc<64, bool mask>",
+                             "frac": tf / pk["bf16_tflops"], "peak": pk["bf16_tflops"],
+                             "peak_kind": pk_kind + " (burst)",
+                             "note": "algorithmic FLOPs of the whole 1024 x 2048 problem; masked-out key tiles are skipped"}
+            del t, m, o
+
+    # Split-KV decode; at N > 1 each rank holds 64 / N batch rows.
+    w = workloads.WORKLOADS["fp16_decode_gqa"]
+    B, Hq, _, D = w.q_shape
+    Hkv, S = w.kv_shape[1], w.kv_shape[2]
+    rows = np.array_split(np.arange(B), world)[rank]
+    b = len(rows)
+    gen = torch.Generator(device=dev).manual_seed(3 + rank)
+    q = (torch.randn((b, Hq, 1, D), generator=gen, device=dev) * 0.5).half()
+    k = (torch.randn((b, Hkv, S, D), generator=gen, device=dev, dtype=torch.float16) * 0.5)
+    v = (torch.randn((b, Hkv, S, D), generator=gen, device=dev, dtype=torch.float16) * 0.5)
+    o = torch.empty_like(q)
+    plan = pa_b200.plan_call(q.shape, k.shape, v.shape, np.float16, np.float16, np.float16, group=Hq // Hkv)
+    nb = ctypes.c_size_t(0)
+    check(lib().pa_decode_workspace_size(ctypes.byref(plan.desc), ctypes.byref(nb)))
+    ws_bytes = int(nb.value)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(dev)
+
+    def dstep():
+        sdpa_device(plan, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), stream=stream,
+                    decode=True, workspace=(ws.data_ptr(), ws_bytes))
+
+    ms = _timed(dstep, 30, 5, stream, pg, local)
+    gbytes = 2.0 * B * Hkv * S * D * 2 + 2.0 * B * Hq * D * 2
+    gbs = gbytes / (ms * 1e-3) / 1e9
+    out["fp16_decode_gqa"] = {"value": gbs, "unit": "GB/s", "ms_per_step": ms,
+                              "kernel": "decode_partial + decode_combine",
+                              "frac": gbs / world / pk["hbm_gbs"], "peak": pk["hbm_gbs"],
+                              "peak_kind": pk_kind + " (per GPU)",
+                              "parallelism": f"batch-shard x{world}" if world > 1 else "single",
+                              "scaling": "strong"}
+    del q, k, v, o, ws
+
+    if world == 1:
+        # Long-context causal forward + backward on one GPU.
+        w = workloads.WORKLOADS["fp16_long_causal"]
+        gen = torch.Generator(device=dev).manual_seed(4)
+        t = {key: torch.randn(w.q_shape, generator=gen, device=dev, dtype=torch.float16)
+             for key in ("q", "k", "v", "dout")}
+        for key in ("out", "dq", "dk", "dv"):
+            t[key] = torch.empty(w.q_shape, device=dev, dtype=torch.float16)
+        lse = torch.empty(w.q_shape[:3], device=dev, dtype=torch.float32)
+        plan = pa_b200.plan_call(w.q_shape, w.kv_shape, w.kv_shape, np.float16, np.float16, np.float16,
+                                 is_causal=True)
+        desc = ctypes.byref(plan.desc)
+        mid = [None]
+        torch.cuda.synchronize(dev)
+
+        def lstep():
+            check(lib().pa_sdpa_fwd(desc, t["q"].data_ptr(), t["k"].data_ptr(), t["v"].data_ptr(), None,
+                                    t["out"].data_ptr(), lse.data_ptr(), stream.handle))
+            if mid[0] is not None:
+                mid[0].record(stream)
+            check(lib().pa_sdpa_bwd(desc, t["q"].data_ptr(), t["k"].data_ptr(), t["v"].data_ptr(),
+                                    t["out"].data_ptr(), t["dout"].data_ptr(), lse.data_ptr(),
+                                    t["dq"].data_ptr(), t["dk"].data_ptr(), t["dv"].data_ptr(),
+                                    stream.handle))
+
+        ms = _timed(lstep, 3, 2, stream, pg, local)
+        e0, mid[0], e1 = Event(), Event(), Event()
+        e0.record(stream)
+        lstep()
+        e1.record(stream)
+        stream.synchronize()
+        fwd_ms, bwd_ms = e0.elapsed_ms(mid[0]), mid[0].elapsed_ms(e1)
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        bwd_tf = w.flops_bwd / (bwd_ms * 1e-3) / 1e12
+        out["fp16_long_causal"] = {
+            "value": (w.flops_fwd + w.flops_bwd) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ms, "fwd_tflops": w.flops_fwd / (fwd_ms * 1e-3) / 1e12,
+            "bwd_tflops": bwd_tf, "bwd_frac": bwd_tf / peak, "peak": peak,
+            "peak_kind": pk_kind + " (sustained: seconds-long step)",
+            "kernel": "fwd_tc + bwd_prep + bwd_dkdv + bwd_dq"}
+        del t, lse
+    torch.cuda.synchronize(dev)
+    return out
 
 
 def ring_subrecord(rank, local, world, pg, steps=3, warmup=2):
@@ -1090,6 +1261,8 @@ def main():
     ap.add_argument("--workload", default="fp16_causal_gqa")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="skip the device-timed lines of the other workloads")
     ap.add_argument("--no-ring", action="store_true",
                     help="N > 1: skip the ring-attention sub-record of the long-context workload")
     ap.add_argument("--clock-dir", default=None,

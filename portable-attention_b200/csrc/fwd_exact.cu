@@ -32,6 +32,7 @@ struct ExactArgs {
   int64_t q_rs, k_rs, v_rs, m_rs, m_cs;
   int64_t nslices;
   int32_t causal;
+  int32_t lt_kv_aligned;  // every k/v slice offset is a multiple of 4 elements
   double scale;
 };
 
@@ -309,6 +310,280 @@ __global__ void __launch_bounds__(kTWarps * 32, 2) sdpa_exact_tiled_kernel(Exact
   store_row(ib, acc_b, m_b, l_b);
 }
 
+// ---------------------------------------------------------------------------
+// Register-tiled fp32 variant for E, Ev <= 128 (fp32, fp16 and bf16 operands;
+// fp64 keeps the kernels above). A CTA of 256 threads owns 64 query rows of
+// one slice and streams 64-key K/V tiles through shared memory (cp.async,
+// double-buffered, when the operands are fp32 with 16-byte rows; converting
+// loads otherwise). Thread (ty, tx) = (tid / 16, tid % 16) computes a 4 x 4
+// block of scores (rows ty + 16a, keys tx + 16b: each warp reads two q rows
+// as broadcasts and sixteen key rows without bank conflicts) and a 4 x NCO
+// block of the output (rows ty + 16a, columns 4tx.. and 64 + 4tx..), so every
+// value read from shared memory feeds four to eight FMAs. The softmax runs in
+// log2 units (q pre-scaled by scale * log2 e, library exp2f); a row's running
+// max is reduced over its 16 threads with shuffles, and its running sum stays
+// split over them until the end (the rescale factor is common to the row).
+// Same semantics as the kernels above: fully-masked rows exactly zero with
+// lse -inf, top-left causal, broadcast boolean / additive masks.
+constexpr int kRBM = 64;       // query rows per CTA
+constexpr int kRBN = 64;       // keys per tile
+constexpr int kRThreads = 256;
+constexpr int kRMaxDim = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__host__ __device__ constexpr int rt_qpitch(int e) { return ((e + 3) & ~3) + 4; }
+__host__ __device__ constexpr int rt_vpitch(int ev) { return ev <= 64 ? 64 : 128; }
+constexpr int kRPPitch = kRBM + 4;
+
+__host__ __device__ constexpr size_t rt_smem(int e, int ev) {
+  // sQ + 2 x (sK + sV) + sP, in floats
+  return static_cast<size_t>(kRBM * rt_qpitch(e) + 2 * (kRBN * rt_qpitch(e) + kRBN * rt_vpitch(ev)) +
+                             kRBN * kRPPitch) * sizeof(float);
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = smem_u32(dst);
+  const uint32_t n = valid ? 16u : 0u;  // 0: fill the 16 bytes with zeros, read nothing
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <typename T, int MASK, typename MaskT, int NCO, bool ASYNC>
+__global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_r[];
+  const int E = static_cast<int>(a.E), Ev = static_cast<int>(a.Ev);
+  const int QP = rt_qpitch(E), EP = QP - 4;
+  constexpr int VP = NCO == 4 ? 64 : 128;
+  float* sQ = reinterpret_cast<float*>(smem_r);        // [kRBM][QP]
+  float* sK0 = sQ + kRBM * QP;                          // [2][kRBN][QP]
+  float* sV0 = sK0 + 2 * kRBN * QP;                     // [2][kRBN][VP]
+  float* sP = sV0 + 2 * kRBN * VP;                      // [kRBN][kRPPitch], P^T with rows permuted
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t groups = (a.L + kRBM - 1) / kRBM;
+  const int64_t slice = blockIdx.x / groups;
+  const int64_t i0 = (blockIdx.x % groups) * kRBM;
+  const SliceOffsets off = slice_offsets(a.lt, slice);
+  const T* qb = static_cast<const T*>(a.q) + off.q;
+  const T* kb = static_cast<const T*>(a.k) + off.k;
+  const T* vb = static_cast<const T*>(a.v) + off.v;
+  const float qscale = static_cast<float>(a.scale) * kLog2e;
+  const float neg_inf = -INFINITY;
+  const int64_t last_row = (i0 + kRBM < a.L ? i0 + kRBM : a.L) - 1;
+  const int64_t cta_end = a.causal ? (last_row + 1 < a.S ? last_row + 1 : a.S) : a.S;
+  const int ntiles = static_cast<int>((cta_end + kRBN - 1) / kRBN);
+
+  // Q rows, pre-scaled, zero-padded; V padding columns zeroed once (never stored,
+  // but they must be finite).
+  for (int idx = tid; idx < kRBM * QP; idx += kRThreads) {
+    const int r = idx / QP, e = idx % QP;
+    const int64_t row = i0 + r;
+    sQ[idx] = (e < E && row < a.L) ? load_as<float>(qb + row * a.q_rs + e) * qscale : 0.f;
+  }
+  if (Ev < VP)
+    for (int idx = tid; idx < 2 * kRBN * VP; idx += kRThreads)
+      if (idx % VP >= Ev) sV0[idx] = 0.f;
+
+  auto load_tile = [&](int t, int buf) {
+    float* sK = sK0 + buf * kRBN * QP;
+    float* sV = sV0 + buf * kRBN * VP;
+    const int64_t j0 = static_cast<int64_t>(t) * kRBN;
+    if (ASYNC) {
+      const int kc = E / 4, vc = Ev / 4;  // 16-byte chunks per row (E, Ev multiples of 4 here)
+      for (int idx = tid; idx < kRBN * kc; idx += kRThreads) {
+        const int r = idx / kc, c = idx % kc;
+        const int64_t key = j0 + r;
+        const bool ok = key < a.S;
+        cp_async16(sK + r * QP + 4 * c, kb + (ok ? key : 0) * a.k_rs + 4 * c, ok);
+      }
+      for (int idx = tid; idx < kRBN * vc; idx += kRThreads) {
+        const int r = idx / vc, c = idx % vc;
+        const int64_t key = j0 + r;
+        const bool ok = key < a.S;
+        cp_async16(sV + r * VP + 4 * c, vb + (ok ? key : 0) * a.v_rs + 4 * c, ok);
+      }
+    } else {
+      for (int idx = tid; idx < kRBN * EP; idx += kRThreads) {
+        const int r = idx / EP, e = idx % EP;
+        const int64_t key = j0 + r;
+        sK[r * QP + e] = (key < a.S && e < E) ? load_as<float>(kb + key * a.k_rs + e) : 0.f;
+      }
+      for (int idx = tid; idx < kRBN * Ev; idx += kRThreads) {
+        const int r = idx / Ev, c = idx % Ev;
+        const int64_t key = j0 + r;
+        sV[r * VP + c] = key < a.S ? load_as<float>(vb + key * a.v_rs + c) : 0.f;
+      }
+    }
+  };
+
+  float o[4][NCO];
+  float m[4], l[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    m[r] = neg_inf;
+    l[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCO; ++c) o[r][c] = 0.f;
+  }
+
+  if (ASYNC && ntiles > 0) {
+    load_tile(0, 0);
+    cp_async_commit();
+  }
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    __syncthreads();  // the previous tile's P and V reads are done (and sQ is written)
+    if (ASYNC) {
+      if (t + 1 < ntiles) load_tile(t + 1, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();  // this thread's copies of tile t have landed
+    } else {
+      load_tile(t, buf);
+    }
+    __syncthreads();
+    const float* sK = sK0 + buf * kRBN * QP;
+    const float* sV = sV0 + buf * kRBN * VP;
+    const int64_t j0 = static_cast<int64_t>(t) * kRBN;
+
+    float s[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) s[r][b] = 0.f;
+    for (int e = 0; e < EP; e += 4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) qv[r] = *reinterpret_cast<const float4*>(sQ + (ty + 16 * r) * QP + e);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) kv[b] = *reinterpret_cast<const float4*>(sK + (tx + 16 * b) * QP + e);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          s[r][b] = fmaf(qv[r].x, kv[b].x, s[r][b]);
+          s[r][b] = fmaf(qv[r].y, kv[b].y, s[r][b]);
+          s[r][b] = fmaf(qv[r].z, kv[b].z, s[r][b]);
+          s[r][b] = fmaf(qv[r].w, kv[b].w, s[r][b]);
+        }
+    }
+
+    // Mask, online softmax (log2 units), P^T into shared memory.
+    float alpha[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int64_t row = i0 + ty + 16 * r;
+      const int64_t vis = a.causal ? (row + 1 < a.S ? row + 1 : a.S) : a.S;
+      float mt = neg_inf;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int64_t key = j0 + tx + 16 * b;
+        float x = (key < vis && row < a.L) ? s[r][b] : neg_inf;
+        if (MASK != PA_MASK_NONE && x != neg_inf) {
+          const int64_t mo = off.m + row * a.m_rs + key * a.m_cs;
+          if (MASK == PA_MASK_BOOL) {
+            if (!static_cast<const uint8_t*>(a.mask)[mo]) x = neg_inf;
+          } else {
+            x = fmaf(load_as<float>(static_cast<const MaskT*>(a.mask) + mo), kLog2e, x);
+          }
+        }
+        s[r][b] = x;
+        mt = fmaxf(mt, x);
+      }
+#pragma unroll
+      for (int sh = 8; sh; sh >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, sh));
+      const float m_new = fmaxf(m[r], mt);
+      if (m_new == neg_inf) {  // every key so far masked: nothing accumulates
+        alpha[r] = 1.f;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) s[r][b] = 0.f;
+      } else {
+        alpha[r] = exp2f(m[r] - m_new);  // 0 when m[r] is -inf
+        float ps = 0.f;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          s[r][b] = exp2f(s[r][b] - m_new);
+          ps += s[r][b];
+        }
+        l[r] = l[r] * alpha[r] + ps;
+        m[r] = m_new;
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      *reinterpret_cast<float4*>(sP + (tx + 16 * b) * kRPPitch + 4 * ty) =
+          make_float4(s[0][b], s[1][b], s[2][b], s[3][b]);
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < NCO; ++c) o[r][c] *= alpha[r];
+    __syncthreads();
+
+    const int nk = static_cast<int>(cta_end - j0 < kRBN ? cta_end - j0 : kRBN);
+    for (int k = 0; k < nk; ++k) {
+      const float4 pv = *reinterpret_cast<const float4*>(sP + k * kRPPitch + 4 * ty);
+      const float p4[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+      for (int g = 0; g < NCO / 4; ++g) {
+        const float4 vv = *reinterpret_cast<const float4*>(sV + k * VP + 64 * g + 4 * tx);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          o[r][4 * g + 0] = fmaf(p4[r], vv.x, o[r][4 * g + 0]);
+          o[r][4 * g + 1] = fmaf(p4[r], vv.y, o[r][4 * g + 1]);
+          o[r][4 * g + 2] = fmaf(p4[r], vv.z, o[r][4 * g + 2]);
+          o[r][4 * g + 3] = fmaf(p4[r], vv.w, o[r][4 * g + 3]);
+        }
+      }
+    }
+  }
+
+  // Row sums over the row's 16 threads, then normalise and store.
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    float lr = l[r];
+#pragma unroll
+    for (int sh = 8; sh; sh >>= 1) lr += __shfl_xor_sync(0xffffffffu, lr, sh);
+    const int64_t row = i0 + ty + 16 * r;
+    if (row >= a.L) continue;
+    const float inv = lr > 0.f ? 1.f / lr : 0.f;
+    T* orow = static_cast<T*>(a.out) + (slice * a.L + row) * a.Ev;
+#pragma unroll
+    for (int g = 0; g < NCO / 4; ++g)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int col = 64 * g + 4 * tx + c;
+        if (col < Ev) orow[col] = from_acc<T>(static_cast<double>(lr > 0.f ? o[r][4 * g + c] * inv : 0.f));
+      }
+    if (a.lse && tx == 0)
+      a.lse[slice * a.L + row] = lr > 0.f ? (m[r] + log2f(lr)) * 0.6931471805599453f : -INFINITY;
+  }
+}
+
+template <typename T, int MASK, typename MaskT, int NCO, bool ASYNC>
+pa_status launch_rt_v(const ExactArgs& a, cudaStream_t st) {
+  auto kern = sdpa_exact_rt_kernel<T, MASK, MaskT, NCO, ASYNC>;
+  static uint64_t attr_set = 0;
+  PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern),
+                            static_cast<int>(rt_smem(kRMaxDim, NCO == 4 ? 64 : 128)), &attr_set));
+  const int64_t blocks = a.nslices * ((a.L + kRBM - 1) / kRBM);
+  if (blocks > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "problem too large for the exact kernel");
+  const size_t smem = rt_smem(static_cast<int>(a.E), NCO == 4 ? 64 : 128);
+  kern<<<static_cast<unsigned>(blocks), kRThreads, smem, st>>>(a);
+  PA_CUDA(cudaGetLastError());
+  return PA_OK;
+}
+
+template <typename T, int MASK, typename MaskT>
+pa_status launch_rt(const ExactArgs& a, cudaStream_t st) {
+  // cp.async needs fp32 rows of whole 16-byte chunks at 16-byte aligned addresses.
+  const bool async = sizeof(T) == 4 && a.E % 4 == 0 && a.Ev % 4 == 0 && a.k_rs % 4 == 0 &&
+                     a.v_rs % 4 == 0 && (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 && a.lt_kv_aligned;
+  if (a.Ev <= 64)
+    return async ? launch_rt_v<T, MASK, MaskT, 4, true>(a, st) : launch_rt_v<T, MASK, MaskT, 4, false>(a, st);
+  return async ? launch_rt_v<T, MASK, MaskT, 8, true>(a, st) : launch_rt_v<T, MASK, MaskT, 8, false>(a, st);
+}
+
 template <typename T, typename Acc, int MASK, typename MaskT, int NC>
 pa_status launch_tiled_nc(const ExactArgs& a, cudaStream_t st) {
   auto kern = sdpa_exact_tiled_kernel<T, Acc, MASK, MaskT, NC>;
@@ -336,6 +611,17 @@ pa_status launch_typed(const ExactArgs& a, const pa_sdpa_desc& d, cudaStream_t s
   const int64_t blocks = a.nslices * ((a.L + kWarps - 1) / kWarps);
   if (blocks > 0x7fffffffLL) return fail(PA_ERR_UNSUPPORTED, "problem too large for the exact kernel");
   dim3 grid(static_cast<unsigned>(blocks)), block(kWarps * 32);
+  if (sizeof(Acc) == 4 && a.E <= kRMaxDim && a.Ev <= kRMaxDim && a.L > 0) {
+    if (d.mask_kind == PA_MASK_NONE || d.is_causal) return launch_rt<T, PA_MASK_NONE, float>(a, st);
+    if (d.mask_kind == PA_MASK_BOOL) return launch_rt<T, PA_MASK_BOOL, uint8_t>(a, st);
+    switch (d.mask_dtype) {
+      case PA_F16: return launch_rt<T, PA_MASK_ADD, __half>(a, st);
+      case PA_BF16: return launch_rt<T, PA_MASK_ADD, __nv_bfloat16>(a, st);
+      case PA_F32: return launch_rt<T, PA_MASK_ADD, float>(a, st);
+      case PA_F64: return launch_rt<T, PA_MASK_ADD, double>(a, st);
+      default: return fail(PA_ERR_INVALID, "unsupported additive mask dtype");
+    }
+  }
   if (a.E <= kTMaxDim && a.Ev <= kTMaxDim && a.L > 0) {
     if (d.mask_kind == PA_MASK_NONE || d.is_causal) return launch_tiled<T, Acc, PA_MASK_NONE, float>(a, st);
     if (d.mask_kind == PA_MASK_BOOL) return launch_tiled<T, Acc, PA_MASK_BOOL, uint8_t>(a, st);
@@ -377,6 +663,9 @@ pa_status launch_fwd_exact(const pa_sdpa_desc& d, const void* q, const void* k, 
   a.nslices = lead_count(d);
   a.causal = d.is_causal;
   a.scale = d.scale;
+  a.lt_kv_aligned = 1;
+  for (int i = 0; i < d.nlead; ++i)
+    if (d.k_lead_stride[i] % 4 || d.v_lead_stride[i] % 4) a.lt_kv_aligned = 0;
   switch (d.dtype) {
     case PA_F64: return launch_typed<double, double>(a, d, st);
     case PA_F32: return launch_typed<float, float>(a, d, st);
