@@ -350,11 +350,13 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <typename T, int MASK, typename MaskT, int NCO, bool ASYNC>
+template <typename T, int MASK, typename MaskT, int NCO, bool ASYNC, int EPT>
 __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a) {
   extern __shared__ __align__(16) uint8_t smem_r[];
-  const int E = static_cast<int>(a.E), Ev = static_cast<int>(a.Ev);
-  const int QP = rt_qpitch(E), EP = QP - 4;
+  // EPT != 0: the head dimension is EPT (a multiple of 4), known at compile time
+  // so the score loop unrolls completely.
+  const int E = EPT ? EPT : static_cast<int>(a.E), Ev = static_cast<int>(a.Ev);
+  const int QP = EPT ? EPT + 4 : rt_qpitch(E), EP = QP - 4;
   constexpr int VP = NCO == 4 ? 64 : 128;
   float* sQ = reinterpret_cast<float*>(smem_r);        // [kRBM][QP]
   float* sK0 = sQ + kRBM * QP;                          // [2][kRBN][QP]
@@ -451,6 +453,7 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int b = 0; b < 4; ++b) s[r][b] = 0.f;
+#pragma unroll
     for (int e = 0; e < EP; e += 4) {
       float4 qv[4], kv[4];
 #pragma unroll
@@ -520,6 +523,7 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
     __syncthreads();
 
     const int nk = static_cast<int>(cta_end - j0 < kRBN ? cta_end - j0 : kRBN);
+#pragma unroll 4
     for (int k = 0; k < nk; ++k) {
       const float4 pv = *reinterpret_cast<const float4*>(sP + k * kRPPitch + 4 * ty);
       const float p4[4] = {pv.x, pv.y, pv.z, pv.w};
@@ -559,9 +563,9 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
   }
 }
 
-template <typename T, int MASK, typename MaskT, int NCO, bool ASYNC>
+template <typename T, int MASK, typename MaskT, int NCO, bool ASYNC, int EPT = 0>
 pa_status launch_rt_v(const ExactArgs& a, cudaStream_t st) {
-  auto kern = sdpa_exact_rt_kernel<T, MASK, MaskT, NCO, ASYNC>;
+  auto kern = sdpa_exact_rt_kernel<T, MASK, MaskT, NCO, ASYNC, EPT>;
   static uint64_t attr_set = 0;
   PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern),
                             static_cast<int>(rt_smem(kRMaxDim, NCO == 4 ? 64 : 128)), &attr_set));
@@ -579,6 +583,8 @@ pa_status launch_rt(const ExactArgs& a, cudaStream_t st) {
   const bool async = sizeof(T) == 4 && a.E % 4 == 0 && a.Ev % 4 == 0 && a.k_rs % 4 == 0 &&
                      a.v_rs % 4 == 0 && (reinterpret_cast<uintptr_t>(a.k) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(a.v) & 15) == 0 && a.lt_kv_aligned;
+  if (MASK == PA_MASK_NONE && async && a.Ev <= 64 && a.E == 64) return launch_rt_v<T, MASK, MaskT, 4, true, 64>(a, st);
+  if (MASK == PA_MASK_NONE && async && a.Ev > 64 && a.E == 128) return launch_rt_v<T, MASK, MaskT, 8, true, 128>(a, st);
   if (a.Ev <= 64)
     return async ? launch_rt_v<T, MASK, MaskT, 4, true>(a, st) : launch_rt_v<T, MASK, MaskT, 4, false>(a, st);
   return async ? launch_rt_v<T, MASK, MaskT, 8, true>(a, st) : launch_rt_v<T, MASK, MaskT, 8, false>(a, st);
