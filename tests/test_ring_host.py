@@ -5,8 +5,10 @@ The GPU ring (``pa_ring_fwd`` / ``pa_ring_bwd``) follows the schedule of
 float64 simulation of the whole ring (``oracle/ring.py``) is checked against
 the oracle forward and VJP on the gathered sequence for 1-4 ranks, and a
 world-size-2 ``gloo`` job runs the same algorithm with real point-to-point
-messages between processes and the NCCL-id exchange of ``RingComm`` against a
-fake native library.
+messages between processes (the forward, and the backward in the native
+schedule's message order, accumulators travelling with their key/value block
+and coming home after the last step) and the NCCL-id exchange of ``RingComm``
+against a fake native library.
 """
 
 from __future__ import annotations
@@ -17,7 +19,7 @@ import socket
 import numpy as np
 import pytest
 
-from oracle.ring import block_attention, simulate_ring
+from oracle.ring import block_attention, block_grads, simulate_ring
 from oracle.sdpa import reference_sdpa
 from oracle.vjp import reference_vjp
 from pa_b200.ring import owned_chunks, ring_pairs, shard, unshard
@@ -140,17 +142,60 @@ def _worker(rank, world, port, result_path):
         if rank == 0:
             np.testing.assert_allclose(unshard(outs), reference_sdpa(q, k, v, is_causal=True),
                                        rtol=1e-12, atol=1e-12)
+
+        # Backward with the native message schedule (csrc/ring.cu pa_ring_bwd): per step
+        # the K/V group for the next step, this step's pairs, then one group that sends the
+        # held block's dK/dV accumulators on to r+1 and receives, from r-1, those of the
+        # block held next (after the last step: this rank's own block, home).
+        do = rng.standard_normal(q.shape)
+        dos = shard(do, n, rank)
+        held = torch.from_numpy(np.concatenate([ks, vs], axis=-1).copy())
+        acc = torch.zeros_like(held)          # dK | dV of the held block
+        dq = np.zeros(qs.shape)
+        for t in range(n):
+            if t + 1 < n:
+                nxt = torch.empty_like(held)
+                kv_reqs = [dist.isend(held, (rank + 1) % n), dist.irecv(nxt, (rank - 1) % n)]
+            kv = held.numpy()
+            hk, hv = kv[..., :D], kv[..., D:]
+            a = acc.numpy()
+            for qsl, ksl, causal in ring_pairs(n, rank, t):
+                rows = slice(qsl * C, (qsl + 1) * C)
+                cols = slice(ksl * C, (ksl + 1) * C)
+                gq, gk, gv = block_grads(qs[..., rows, :], hk[..., cols, :], hv[..., cols, :],
+                                         dos[..., rows, :], acc_o[..., rows, :], acc_l[..., rows],
+                                         causal, scale)
+                dq[..., rows, :] += gq
+                a[..., cols, :D] += gk
+                a[..., cols, D:] += gv
+            if n > 1:
+                nacc = torch.empty_like(acc)
+                acc_reqs = [dist.isend(acc, (rank + 1) % n), dist.irecv(nacc, (rank - 1) % n)]
+                for rq in acc_reqs:
+                    rq.wait()
+                acc = nacc
+            if t + 1 < n:
+                for rq in kv_reqs:
+                    rq.wait()
+                held = nxt
+        grads = [None] * world
+        dist.all_gather_object(grads, (dq, acc.numpy()[..., :D].copy(), acc.numpy()[..., D:].copy()))
+        if rank == 0:
+            wq, wk, wv = reference_vjp(q, k, v, do, is_causal=True)
+            for i, want in enumerate((wq, wk, wv)):
+                np.testing.assert_allclose(unshard([g[i] for g in grads]), want, rtol=1e-10, atol=1e-12)
             with open(result_path, "w") as f:
                 f.write("ok")
     finally:
         dist.destroy_process_group()
 
 
-def test_two_rank_gloo_ring(tmp_path):
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_ring(tmp_path, world):
     import torch.multiprocessing as mp
 
     result = tmp_path / "result.txt"
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    mp.start_processes(_worker, args=(2, _free_port(), str(result)), nprocs=2, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), str(result)), nprocs=world, join=True,
                        start_method="spawn")
     assert result.read_text() == "ok"
