@@ -599,10 +599,18 @@ def run_gpu(args):
         work = fwd_flops(x, w)
         value = global_flops / (ms * 1e-3) / 1e12
         achieved = work / (statistics.mean(per) * 1e-3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
-                "traffic": traffic_for(args.workload), "peak_kind": pk_kind + " (burst)",
-                "kernel": "fwd_tc" if plan.cdt == np.float16 else "sdpa_exact"}
+        if plan.cdt in (np.float16,):
+            roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                    "traffic": traffic_for(args.workload), "peak_kind": pk_kind + " (burst)",
+                    "kernel": "fwd_tc"}
+        else:
+            # fp32 on CUDA cores (FFMA, no TF32): no measured fp32 peak exists.
+            roof = {"bound": "fp32 ffma", "achieved": achieved, "peak": FP32_FFMA_PEAK_TFLOPS,
+                    "unit": "TFLOP/s", "frac": achieved / FP32_FFMA_PEAK_TFLOPS,
+                    "traffic": traffic_for(args.workload),
+                    "peak_kind": "theoretical (148 SMs x 128 FFMA lanes x 2 x 1965 MHz)",
+                    "kernel": "sdpa_exact_rt"}
         # a boolean mask adds the tile-classification pre-pass
         launches = 2 if (mask is not None and mask.dtype == np.bool_) else 1
 
@@ -780,11 +788,12 @@ def workload_subrecords(rank, local, world, pg):
             tf = w.flops_fwd / (ms * 1e-3) / 1e12
             if name == "fp32_unmasked":
                 out[name] = {"value": tf, "unit": "TFLOP/s", "ms_per_step": ms, "kernel": "sdpa_exact_rt (fp32 FFMA)",
+                             "traffic": traffic_for(name),
                              "frac_of_fp32_ffma_theoretical": tf / FP32_FFMA_PEAK_TFLOPS,
                              "peak_note": "148 SMs x 128 FFMA lanes x 2 x 1965 MHz; no measured fp32 peak"}
             else:
                 out[name] = {"value": tf, "unit": "TFLOP/s", "ms_per_step": ms,
-                             "kernel": "mask_classify + fwd_tc<64, bool mask>",
+                             "kernel": "mask_classify + fwd_tc<64, bool mask>", "traffic": traffic_for(name),
                              "frac": tf / pk["bf16_tflops"], "peak": pk["bf16_tflops"],
                              "peak_kind": pk_kind + " (burst)",
                              "note": "algorithmic FLOPs of the whole 1024 x 2048 problem; masked-out key tiles are skipped"}
@@ -817,6 +826,7 @@ def workload_subrecords(rank, local, world, pg):
     gbs = gbytes / (ms * 1e-3) / 1e9
     out["fp16_decode_gqa"] = {"value": gbs, "unit": "GB/s", "ms_per_step": ms,
                               "kernel": "decode_partial + decode_combine",
+                              "traffic": traffic_for("fp16_decode_gqa") if world == 1 else None,
                               "frac": gbs / world / pk["hbm_gbs"], "peak": pk["hbm_gbs"],
                               "peak_kind": pk_kind + " (per GPU)",
                               "parallelism": f"batch-shard x{world}" if world > 1 else "single",
