@@ -30,6 +30,8 @@
 // -inf (fully masked) have P = 0 and so zero gradient.
 #include <math.h>
 
+#include <functional>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -47,6 +49,12 @@ struct BwdArgs {
   void* dk;
   void* dv;
   void* dq;
+  // When set, the gradients are added in fp32 into these (same dense layouts as
+  // dk / dv / dq) instead of being stored in the operand type: the ring
+  // accumulates a chunk pair's contribution this way without extra kernels.
+  float* dk_acc;
+  float* dv_acc;
+  float* dq_acc;
   const void* q;       // (slices_q, L, D), read row by row into tensor memory by the dQ kernel
   const void* dout;    // same layout as q
   const float* lse2;   // [slices_q][Lp], log2 units
@@ -102,6 +110,20 @@ __global__ void bwd_prep_kernel(const void* o, const void* dout, const float* ls
     delta[r] = acc;
     const float l = lse[sl * L + row];
     lse2[r] = l == -INFINITY ? -INFINITY : l * 1.4426950408889634f;
+  }
+}
+
+// Add 32 fp32 values (scaled) into 32 consecutive fp32 accumulators (16-byte aligned).
+__device__ __forceinline__ void accum_row32(float* dst, const uint32_t (&rr)[32], float mul) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    float4 x = d4[t];
+    x.x = fmaf(__uint_as_float(rr[4 * t]), mul, x.x);
+    x.y = fmaf(__uint_as_float(rr[4 * t + 1]), mul, x.y);
+    x.z = fmaf(__uint_as_float(rr[4 * t + 2]), mul, x.z);
+    x.w = fmaf(__uint_as_float(rr[4 * t + 3]), mul, x.w);
+    d4[t] = x;
   }
 }
 
@@ -378,7 +400,10 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 #pragma unroll
           for (int t = 0; t < 32; ++t) rv[t] = rk[t] = 0u;
         }
-        if (row_ok) {
+        if (row_ok && a.dk_acc) {
+          accum_row32(a.dv_acc + (pair * a.S + key) * D + c * 32, rv, 1.f);
+          accum_row32(a.dk_acc + (pair * a.S + key) * D + c * 32, rk, a.scale);
+        } else if (row_ok) {
           store_row32<BF16>(dvrow + c * 64, rv, 1.f);
           store_row32<BF16>(dkrow + c * 64, rk, a.scale);
         }
@@ -637,7 +662,8 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 #pragma unroll
           for (int t = 0; t < 32; ++t) rq[t] = 0u;
         }
-        if (row < a.L) store_row32<BF16>(dqrow + c * 64, rq, a.scale);
+        if (row < a.L && a.dq_acc) accum_row32(a.dq_acc + (zq * a.L + row) * D + c * 32, rq, a.scale);
+        else if (row < a.L) store_row32<BF16>(dqrow + c * 64, rq, a.scale);
       }
     }
   }
@@ -652,7 +678,9 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 template <int D, bool BF16>
 pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv, const void* q,
                         const void* k, const void* v, const void* o, const void* dout,
-                        const float* lse, void* dq, void* dk, void* dv, cudaStream_t st) {
+                        const float* lse, void* dq, void* dk, void* dv, cudaStream_t st,
+                        float* dq_acc = nullptr, float* dk_acc = nullptr, float* dv_acc = nullptr,
+                        const std::function<void()>* before_dkdv = nullptr) {
   const int64_t L = d.L, S = d.S;
   const int64_t Lp = (L + kRowPad - 1) / kRowPad * kRowPad;
   const int64_t nkv = (n / H) * Hkv;
@@ -685,6 +713,9 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
     a.dk = dk;
     a.dv = dv;
     a.dq = dq;
+    a.dk_acc = dk_acc;
+    a.dv_acc = dv_acc;
+    a.dq_acc = dq_acc;
     a.q = q;
     a.dout = dout;
     a.lse2 = lse2;
@@ -703,33 +734,42 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
     a.causal = d.is_causal;
     a.scale_log2 = static_cast<float>(d.scale * 1.4426950408889634);
     a.scale = static_cast<float>(d.scale);
-    {
+    auto run_dkdv = [&]() -> pa_status {
       using C = DkdvCfg<D>;
-      a.slices = nkv;
-      a.blocks = static_cast<int32_t>((S + C::BK - 1) / C::BK);
-      const int64_t grid = nkv * a.blocks;
+      BwdArgs b = a;
+      b.slices = nkv;
+      b.blocks = static_cast<int32_t>((S + C::BK - 1) / C::BK);
+      const int64_t grid = nkv * b.blocks;
       auto kern = bwd_dkdv_kernel<D, BF16>;
       static uint64_t attr_set = 0;
-      if ((rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), C::kSmemBytes, &attr_set)) != PA_OK) break;
-      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tq64, tdo64, tk128, tv128, a);
-      if (cudaGetLastError() != cudaSuccess) {
-        rc = fail(PA_ERR_CUDA, "bwd_dkdv launch failed");
-        break;
-      }
-    }
-    {
+      PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), C::kSmemBytes, &attr_set));
+      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tq64, tdo64, tk128, tv128, b);
+      if (cudaGetLastError() != cudaSuccess) return fail(PA_ERR_CUDA, "bwd_dkdv launch failed");
+      return PA_OK;
+    };
+    auto run_dq = [&]() -> pa_status {
       using C = DqCfg<D>;
-      a.slices = n;
-      a.blocks = static_cast<int32_t>((L + C::BQ - 1) / C::BQ);
-      const int64_t grid = n * a.blocks;
+      BwdArgs b = a;
+      b.slices = n;
+      b.blocks = static_cast<int32_t>((L + C::BQ - 1) / C::BQ);
+      const int64_t grid = n * b.blocks;
       auto kern = bwd_dq_kernel<D, BF16>;
       static uint64_t attr_set = 0;
-      if ((rc = set_smem_attr_once(reinterpret_cast<const void*>(kern), C::kSmemBytes, &attr_set)) != PA_OK) break;
-      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tk64, tv64, a);
-      if (cudaGetLastError() != cudaSuccess) {
-        rc = fail(PA_ERR_CUDA, "bwd_dq launch failed");
-        break;
-      }
+      PA_TRY(set_smem_attr_once(reinterpret_cast<const void*>(kern), C::kSmemBytes, &attr_set));
+      if (grid > 0) kern<<<static_cast<unsigned>(grid), kThreadsB, C::kSmemBytes, st>>>(tk64, tv64, b);
+      if (cudaGetLastError() != cudaSuccess) return fail(PA_ERR_CUDA, "bwd_dq launch failed");
+      return PA_OK;
+    };
+    if (before_dkdv) {
+      // Accumulating into buffers that may still be arriving: dQ first (its
+      // accumulator is the caller's own), then whatever the caller must wait for,
+      // then dK/dV.
+      if ((rc = run_dq()) != PA_OK) break;
+      if (*before_dkdv) (*before_dkdv)();
+      rc = run_dkdv();
+    } else {
+      if ((rc = run_dkdv()) != PA_OK) break;
+      rc = run_dq();
     }
   } while (false);
   scratch_free(ws, st);
@@ -737,6 +777,30 @@ pa_status launch_bwd_tc(const pa_sdpa_desc& d, int64_t n, int64_t H, int64_t Hkv
 }
 
 }  // namespace
+
+pa_status bwd_accumulate(const pa_sdpa_desc& d, const void* q, const void* k, const void* v,
+                         const void* out, const void* dout, const float* lse, float* dq_acc,
+                         float* dk_acc, float* dv_acc, cudaStream_t st,
+                         const std::function<void()>& before_dkdv) {
+  std::string why;
+  if (d.mask_kind != PA_MASK_NONE || !fwd_tc_eligible(d, &why))
+    return fail(PA_ERR_UNSUPPORTED, "backward accumulate: dense fp16/bf16 (B, H, L, D), D in {64, 128}, no mask");
+  if (!dq_acc || !dk_acc || !dv_acc) return fail(PA_ERR_INVALID, "backward accumulate: null accumulator");
+  int64_t n, H, Hkv;
+  dense_bhsd(d, &n, &H, &Hkv);
+  if (n == 0 || d.L == 0 || d.S == 0) return PA_OK;  // nothing to add
+  const bool bf16 = d.dtype == PA_BF16;
+  if (d.E == 128)
+    return bf16 ? launch_bwd_tc<128, true>(d, n, H, Hkv, q, k, v, out, dout, lse, nullptr, nullptr, nullptr, st,
+                                           dq_acc, dk_acc, dv_acc, &before_dkdv)
+                : launch_bwd_tc<128, false>(d, n, H, Hkv, q, k, v, out, dout, lse, nullptr, nullptr, nullptr, st,
+                                            dq_acc, dk_acc, dv_acc, &before_dkdv);
+  return bf16 ? launch_bwd_tc<64, true>(d, n, H, Hkv, q, k, v, out, dout, lse, nullptr, nullptr, nullptr, st,
+                                        dq_acc, dk_acc, dv_acc, &before_dkdv)
+              : launch_bwd_tc<64, false>(d, n, H, Hkv, q, k, v, out, dout, lse, nullptr, nullptr, nullptr, st,
+                                         dq_acc, dk_acc, dv_acc, &before_dkdv);
+}
+
 }  // namespace pa
 
 using namespace pa;

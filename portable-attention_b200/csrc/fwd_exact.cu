@@ -419,14 +419,15 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
     }
   };
 
-  float o[4][NCO];
+  // Output accumulators as packed pairs of adjacent columns (f32x2 FMAs).
+  uint64_t o2[4][NCO / 2];
   float m[4], l[4];
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     m[r] = neg_inf;
     l[r] = 0.f;
 #pragma unroll
-    for (int c = 0; c < NCO; ++c) o[r][c] = 0.f;
+    for (int c = 0; c < NCO / 2; ++c) o2[r][c] = 0ull;
   }
 
   if (ASYNC && ntiles > 0) {
@@ -448,11 +449,13 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
     const float* sV = sV0 + buf * kRBN * VP;
     const int64_t j0 = static_cast<int64_t>(t) * kRBN;
 
-    float s[4][4];
+    // Scores: each (row, key) keeps two partial sums (even / odd head-dim
+    // terms) in one packed pair, so a 16-byte q and k load feed two f32x2 FMAs.
+    uint64_t s2[4][4];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
-      for (int b = 0; b < 4; ++b) s[r][b] = 0.f;
+      for (int b = 0; b < 4; ++b) s2[r][b] = 0ull;
 #pragma unroll
     for (int e = 0; e < EP; e += 4) {
       float4 qv[4], kv[4];
@@ -464,12 +467,15 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
       for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          s[r][b] = fmaf(qv[r].x, kv[b].x, s[r][b]);
-          s[r][b] = fmaf(qv[r].y, kv[b].y, s[r][b]);
-          s[r][b] = fmaf(qv[r].z, kv[b].z, s[r][b]);
-          s[r][b] = fmaf(qv[r].w, kv[b].w, s[r][b]);
+          s2[r][b] = fma2(f2(qv[r].x, qv[r].y), f2(kv[b].x, kv[b].y), s2[r][b]);
+          s2[r][b] = fma2(f2(qv[r].z, qv[r].w), f2(kv[b].z, kv[b].w), s2[r][b]);
         }
     }
+    float s[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) s[r][b] = f2_lo(s2[r][b]) + f2_hi(s2[r][b]);
 
     // Mask, online softmax (log2 units), P^T into shared memory.
     float alpha[4];
@@ -517,25 +523,26 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
       *reinterpret_cast<float4*>(sP + (tx + 16 * b) * kRPPitch + 4 * ty) =
           make_float4(s[0][b], s[1][b], s[2][b], s[3][b]);
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < 4; ++r) {
+      const uint64_t al2 = f2(alpha[r], alpha[r]);
 #pragma unroll
-      for (int c = 0; c < NCO; ++c) o[r][c] *= alpha[r];
+      for (int c = 0; c < NCO / 2; ++c) o2[r][c] = mul2(o2[r][c], al2);
+    }
     __syncthreads();
 
     const int nk = static_cast<int>(cta_end - j0 < kRBN ? cta_end - j0 : kRBN);
 #pragma unroll 4
     for (int k = 0; k < nk; ++k) {
       const float4 pv = *reinterpret_cast<const float4*>(sP + k * kRPPitch + 4 * ty);
-      const float p4[4] = {pv.x, pv.y, pv.z, pv.w};
+      const uint64_t pd[4] = {f2(pv.x, pv.x), f2(pv.y, pv.y), f2(pv.z, pv.z), f2(pv.w, pv.w)};
 #pragma unroll
       for (int g = 0; g < NCO / 4; ++g) {
         const float4 vv = *reinterpret_cast<const float4*>(sV + k * VP + 64 * g + 4 * tx);
+        const uint64_t v01 = f2(vv.x, vv.y), v23 = f2(vv.z, vv.w);
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          o[r][4 * g + 0] = fmaf(p4[r], vv.x, o[r][4 * g + 0]);
-          o[r][4 * g + 1] = fmaf(p4[r], vv.y, o[r][4 * g + 1]);
-          o[r][4 * g + 2] = fmaf(p4[r], vv.z, o[r][4 * g + 2]);
-          o[r][4 * g + 3] = fmaf(p4[r], vv.w, o[r][4 * g + 3]);
+          o2[r][2 * g] = fma2(pd[r], v01, o2[r][2 * g]);
+          o2[r][2 * g + 1] = fma2(pd[r], v23, o2[r][2 * g + 1]);
         }
       }
     }
@@ -556,7 +563,9 @@ __global__ void __launch_bounds__(kRThreads, 2) sdpa_exact_rt_kernel(ExactArgs a
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int col = 64 * g + 4 * tx + c;
-        if (col < Ev) orow[col] = from_acc<T>(static_cast<double>(lr > 0.f ? o[r][4 * g + c] * inv : 0.f));
+        const uint64_t pr = o2[r][2 * g + c / 2];
+        const float ov = (c & 1) ? f2_hi(pr) : f2_lo(pr);
+        if (col < Ev) orow[col] = from_acc<T>(static_cast<double>(lr > 0.f ? ov * inv : 0.f));
       }
     if (a.lse && tx == 0)
       a.lse[slice * a.L + row] = lr > 0.f ? (m[r] + log2f(lr)) * 0.6931471805599453f : -INFINITY;

@@ -10,9 +10,10 @@
 //   the next one from r-1 (ncclSend/ncclRecv, double-buffered). Each pair's
 //   (O, lse) merges into fp32 accumulators by log-sum-exp.
 // Backward: same rotation; each pair runs the tensor-core backward with the
-//   global lse and O of the forward, dQ accumulates locally in fp32, and fp32
-//   dK/dV accumulators travel with their K/V (sent after the step's compute),
-//   taking one extra hop home at the end.
+//   global lse and O of the forward, its kernels adding the pair's dQ, dK, dV
+//   in fp32 straight into accumulators (dQ local, dK/dV travelling with their
+//   K/V, sent after the step's compute and received while the next step's
+//   first dQ kernel runs), one extra hop bringing dK/dV home at the end.
 // Chunks are copied into dense (B, H, C, D) buffers (pitched 2-D copies) so
 // the single-GPU kernels run unchanged on them.
 #include <dlfcn.h>
@@ -139,14 +140,6 @@ __global__ void ring_store_kernel(const float* acc, void* out, int64_t planes, i
   const int64_t dst = (p * plane_stride_rows + row0) * D + rem;
   if (BF16) static_cast<__nv_bfloat16*>(out)[dst] = __float2bfloat16_rn(acc[i]);
   else static_cast<__half*>(out)[dst] = __float2half_rn(acc[i]);
-}
-
-template <bool BF16>
-__global__ void add_to_f32_kernel(const void* src, float* acc, int64_t n) {
-  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (i >= n) return;
-  acc[i] += BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i])
-                 : __half2float(static_cast<const __half*>(src)[i]);
 }
 
 __global__ void fill_f32_kernel(float* p, float v, int64_t n) {
@@ -476,7 +469,7 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
   const size_t ring_bytes = 4 * kvb + 4 * sh.kv_chunk * 4;
   auto align = [](size_t x) { return (x + 255) & ~size_t(255); };
   const size_t bytes = 3 * 2 * align(qb) + 2 * align(rows * 4) + 2 * align(ring_bytes) +
-                       2 * align(rows * D * 4) + 3 * align(qb) + 2 * align(kvb) + 4096;
+                       2 * align(rows * D * 4) + 4096;
   uint8_t* ws = nullptr;
   PA_TRY(scratch_alloc(reinterpret_cast<void**>(&ws), bytes, st));
   size_t off = 0;
@@ -487,9 +480,6 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
   float* lc[2] = {reinterpret_cast<float*>(take(rows * 4)), reinterpret_cast<float*>(take(rows * 4))};
   uint8_t* ring[2] = {take(ring_bytes), take(ring_bytes)};
   float* dq_acc[2] = {reinterpret_cast<float*>(take(rows * D * 4)), reinterpret_cast<float*>(take(rows * D * 4))};
-  uint8_t* pdq = take(qb);
-  uint8_t* pdk = take(kvb);
-  uint8_t* pdv = take(kvb);
   auto kptr = [&](int b, int w) { return ring[b] + w * kvb; };
   auto vptr = [&](int b, int w) { return ring[b] + (2 + w) * kvb; };
   auto dkacc = [&](int b, int w) { return reinterpret_cast<float*>(ring[b] + 4 * kvb) + w * kv_elems; };
@@ -548,25 +538,20 @@ pa_status pa_ring_bwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
           if (kid > qid) continue;
           pa_sdpa_desc cd = chunk_desc(d, C, kid == qid);
           mark(comm, 0, kPhAttn, st);
-          rc = pa_sdpa_bwd(&cd, qc[qw], kptr(cur, kw), vptr(cur, kw), oc[qw], doc[qw], lc[qw], pdq, pdk,
-                           pdv, st);
-          if (rc != PA_OK) break;
-          if (!have_acc) {
+          // The pair's gradients are added in fp32 by the backward kernels' own
+          // epilogues. Its dQ kernel runs first; before the step's first dK/dV
+          // kernel the stream waits for the incoming accumulators, so their
+          // transfer overlaps that dQ kernel.
+          const std::function<void()> wait_acc = [&]() {
+            if (have_acc) return;
             mark(comm, 0, kPhWait, st);
             cudaStreamWaitEvent(st, comm->ev[1], 0);
+            mark(comm, 0, kPhAttn, st);
             have_acc = true;
-          }
-          mark(comm, 0, kPhAccum, st);
-          const unsigned gq = blocks_for(rows * D, 256), gk = blocks_for(kv_elems, 256);
-          if (bf16) {
-            add_to_f32_kernel<true><<<gq, 256, 0, st>>>(pdq, dq_acc[qw], rows * D);
-            add_to_f32_kernel<true><<<gk, 256, 0, st>>>(pdk, dkacc(cur, kw), kv_elems);
-            add_to_f32_kernel<true><<<gk, 256, 0, st>>>(pdv, dvacc(cur, kw), kv_elems);
-          } else {
-            add_to_f32_kernel<false><<<gq, 256, 0, st>>>(pdq, dq_acc[qw], rows * D);
-            add_to_f32_kernel<false><<<gk, 256, 0, st>>>(pdk, dkacc(cur, kw), kv_elems);
-            add_to_f32_kernel<false><<<gk, 256, 0, st>>>(pdv, dvacc(cur, kw), kv_elems);
-          }
+          };
+          rc = bwd_accumulate(cd, qc[qw], kptr(cur, kw), vptr(cur, kw), oc[qw], doc[qw], lc[qw], dq_acc[qw],
+                              dkacc(cur, kw), dvacc(cur, kw), st, wait_acc);
+          if (rc != PA_OK) break;
         }
       }
       if (rc != PA_OK) break;
