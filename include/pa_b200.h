@@ -132,6 +132,13 @@ pa_status pa_stream_sync(void* stream);
 pa_status pa_event_create(void** event);
 pa_status pa_event_destroy(void* event);
 pa_status pa_event_record(void* event, void* stream);
+/* Block the calling host thread until `event` has completed. */
+pa_status pa_event_sync(void* event);
+/* *pinned = 1 when `ptr` lies in page-locked host memory the CUDA runtime knows
+ * (pa_host_alloc, cudaHostAlloc, registered ranges), 0 for ordinary pageable
+ * memory. The NumPy entry point stages pageable inputs through page-locked
+ * buffers itself, since the driver's own staging of pageable copies is slow. */
+pa_status pa_host_is_pinned(const void* ptr, int32_t* pinned);
 /* Make later work on `stream` wait for `event` (cross-stream ordering). */
 pa_status pa_stream_wait_event(void* stream, void* event);
 pa_status pa_event_elapsed_ms(void* start, void* stop, float* ms);

@@ -355,6 +355,25 @@ pa_status pa_event_destroy(void* event) {
   return PA_OK;
 }
 
+pa_status pa_event_sync(void* event) {
+  PA_CUDA(cudaEventSynchronize(static_cast<cudaEvent_t>(event)));
+  return PA_OK;
+}
+
+pa_status pa_host_is_pinned(const void* ptr, int32_t* pinned) {
+  if (!pinned) return fail(PA_ERR_INVALID, "pa_host_is_pinned: null output");
+  *pinned = 0;
+  if (!ptr) return PA_OK;
+  cudaPointerAttributes at{};
+  const cudaError_t e = cudaPointerGetAttributes(&at, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // an address the runtime does not know: not page-locked
+    return PA_OK;
+  }
+  *pinned = at.type == cudaMemoryTypeHost ? 1 : 0;
+  return PA_OK;
+}
+
 pa_status pa_event_record(void* event, void* stream) {
   PA_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream)));
   return PA_OK;

@@ -126,6 +126,8 @@ SIGNATURES = {
     "pa_event_create": [ctypes.POINTER(_P)],
     "pa_event_destroy": [_P],
     "pa_event_record": [_P, _P],
+    "pa_event_sync": [_P],
+    "pa_host_is_pinned": [_P, ctypes.POINTER(_I32)],
     "pa_stream_wait_event": [_P, _P],
     "pa_event_elapsed_ms": [_P, _P, ctypes.POINTER(ctypes.c_float)],
     "pa_sdpa_fwd": [_DESC, _P, _P, _P, _P, _P, _P, _P],

@@ -17,7 +17,7 @@ from ._lib import check, lib
 
 __all__ = [
     "DeviceArena", "DeviceBuffer", "Event", "PinnedPool", "Stream", "current_device",
-    "device_count", "pinned_empty", "set_device", "sync_device_status",
+    "device_count", "is_pinned", "pinned_empty", "set_device", "sync_device_status",
 ]
 
 _ALIGN = 256
@@ -70,6 +70,9 @@ class Event:
         check(lib().pa_event_create(ctypes.byref(h)))
         self.handle = h.value
         self._fin = weakref.finalize(self, lib().pa_event_destroy, h.value)
+
+    def synchronize(self) -> None:
+        check(lib().pa_event_sync(self.handle))
 
     def record(self, stream: Stream | None = None) -> None:
         check(lib().pa_event_record(self.handle, stream.handle if stream else None))
@@ -176,6 +179,13 @@ class PinnedPool:
 
 
 _pool = PinnedPool()
+
+
+def is_pinned(arr: np.ndarray) -> bool:
+    """True when the array's memory is page-locked (fast, asynchronous copies)."""
+    flag = ctypes.c_int32(0)
+    check(lib().pa_host_is_pinned(arr.ctypes.data, ctypes.byref(flag)))
+    return bool(flag.value)
 
 
 def pinned_empty(shape, dtype) -> np.ndarray:
