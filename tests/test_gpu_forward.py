@@ -208,6 +208,26 @@ def test_full_size_workload_rows(cuda_backend, golden_rows, name):
     assert np.all(o >= vmin - 2e-3) and np.all(o <= vmax + 2e-3)
 
 
+def test_pageable_and_page_locked_inputs_give_identical_results(cuda_backend):
+    """Large calls stage pageable inputs through page-locked buffers themselves."""
+    import pa_b200
+    from pa_b200.device import is_pinned
+
+    rng = np.random.default_rng(37)
+    q = rng.standard_normal((6, 8, 2048, 128)).astype(np.float16)
+    k = rng.standard_normal((6, 8, 2048, 128)).astype(np.float16)
+    v = rng.standard_normal((6, 8, 2048, 128)).astype(np.float16)
+    pinned = [pa_b200.pinned_empty(x.shape, x.dtype) for x in (q, k, v)]
+    for dst, src in zip(pinned, (q, k, v)):
+        dst[...] = src
+    assert is_pinned(pinned[0]) and not is_pinned(q)
+    a = cuda_backend(q, k, v, is_causal=True)
+    b = cuda_backend(*pinned, is_causal=True)
+    np.testing.assert_array_equal(a, b)
+    want = reference_sdpa(q[:1, :2], k[:1, :2], v[:1, :2], is_causal=True)
+    np.testing.assert_allclose(a[:1, :2].astype(np.float64), want.astype(np.float64), rtol=2e-3, atol=2e-3)
+
+
 def test_large_call_pipelined_over_batch_chunks_is_bit_identical(cuda_backend):
     """A call above the pipelining threshold is cut into batch chunks (copy-in, compute
     and copy-out overlapped on three streams); every row must equal a single launch's."""

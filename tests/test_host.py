@@ -187,6 +187,12 @@ def test_decode_null_operands_rejected_before_any_launch():
     assert "null" in h.pa_last_error().decode()
 
 
+def test_ordinary_numpy_memory_is_not_reported_pinned():
+    from pa_b200.device import is_pinned
+
+    assert not is_pinned(np.zeros(1024, np.float32))
+
+
 def test_wait_selftest_rejects_out_of_range_limits():
     h = _lib.lib()
     for bad in (0, -5, 1000001):
