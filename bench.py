@@ -13,19 +13,30 @@ default workload is the fp16 causal grouped-query prefill forward, q
   HBM, timed with CUDA events on the launching stream over exactly K steps,
   max over ranks.
 * ``e2e``: the same metric through the public SdpaBackend call on NumPy arrays
-  in page-locked host memory, host->device and device->host copies included.
+  in page-locked host memory, host->device and device->host copies included;
+  ``e2e.pageable`` is the same call on ordinary NumPy arrays.
 * ``roofline``: the dominant kernel's algorithmic FLOPs (bytes) per launch
-  over its average CUDA-event launch time, against MEASURED_PEAKS.json.
-* ``cpu_baseline``: the oracle port of the reference's ``fused`` CPU backend
-  on a bounded sample of the same workload, all host threads, BLAS pinned to
-  one thread per worker (rank 0, N=1 only).
+  over its average CUDA-event launch time, against MEASURED_PEAKS.json (the
+  fp32 workload against the theoretical FFMA rate: no measured fp32 peak).
+* ``workloads`` (default workload only): device-timed lines for the other
+  benchmark configurations -- fp32 exact forward, masked cross-attention,
+  split-KV decode and long-context forward + backward at N = 1; the decode
+  with its batch split over the ranks at N > 1.
+* ``cpu_baseline``: the reference's own ``fused`` CPU backend (byte-compiled
+  by ``oracle/build_ref.py``; the oracle's restatement, labelled ``port``,
+  only when that is missing) on a bounded sample of the same workload, all
+  host threads, BLAS pinned to one thread per worker, plus ``fused`` and
+  ``reference`` on one item at default BLAS threads and at one (rank 0, N=1).
 
-Multi-GPU (torchrun): batch x head shards are independent, so every rank
-runs its own copy of the workload (weak scaling, no data-path collective);
-torch.distributed provides only the barrier and the max-over-ranks timing.
+Multi-GPU (torchrun): the one global problem is cut into N parts (batch rows,
+or whole grouped-query KV-head groups), one per rank, with no data-path
+collective (strong scaling); torch.distributed provides the barrier and the
+max-over-ranks timing. ``ring`` adds the long-context forward + backward as
+ring attention over the same ranks, with a per-phase split of one profiled
+step.
 
-``--impl reference`` times the reference's CPU algorithm (the oracle port of
-``fused``) on the box's host cores on a bounded sample per step.
+``--impl reference`` times the reference's CPU ``fused`` backend the same way
+on the box's host cores, a bounded sample per step.
 
 KV-cache decode workloads (``--workload kv_fp8_decode_gqa``,
 ``kv_paged_decode_gqa``, ``kv_paged_fp8_decode_gqa``) run the decode shapes
