@@ -19,6 +19,10 @@ relative to the portable-attention project root):
   per-case acceptance rule (``src/portable_attention/conformance.py:66-298``).
 * :mod:`oracle.ring` -- an n-rank NumPy simulation of ring attention with a
   log-sum-exp merge, used to check the host-side ring schedule.
+* :mod:`oracle.build_ref` -- byte-compiles the real reference package into
+  ``oracle/_ref`` (git-ignored, carried with the working tree) and imports it
+  from there, so the reference's own conformance kit and CPU backends run
+  where no reference checkout exists (tests, and bench.py's CPU baseline).
 
 Pinning: ``tests/golden/make_golden.py`` imports the real reference package and
 writes its outputs to ``tests/golden/*.npz``; ``tests/test_oracle.py`` checks
