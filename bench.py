@@ -73,7 +73,7 @@ METRIC = "SDPA TFLOP/s (fwd, fwd+bwd) at 1/2/4/8 B200; decode HBM GB/s; %peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
-def clock_log(args, rank: int) -> Path:
+def clock_log(args, rank: int, tag: str = "") -> Path:
     """CSV file for this rank's nvidia-smi clock samples.
 
     ``--clock-dir`` when given; otherwise a fresh private folder per run and
@@ -84,7 +84,7 @@ def clock_log(args, rank: int) -> Path:
         out_dir.mkdir(parents=True, exist_ok=True)
     else:
         out_dir = Path(tempfile.mkdtemp(prefix=f"pa_b200_bench_r{rank}_"))
-    return out_dir / f"clocks_rank{rank}.csv"
+    return out_dir / f"clocks{tag}_rank{rank}.csv"
 
 
 def peaks():
@@ -685,7 +685,7 @@ def run_gpu(args):
     ring = None
     if world > 1 and not args.no_ring and not backward and not decode:
         try:
-            ring = ring_subrecord(rank, local, world, pg)
+            ring = ring_subrecord(rank, local, world, pg, clock_path=clock_log(args, rank, "_ring"))
         except Exception as exc:  # noqa: BLE001 -- keep the main line; every rank fails alike
             ring = {"error": f"{type(exc).__name__}: {exc}"}
 
@@ -889,7 +889,7 @@ def workload_subrecords(rank, local, world, pg):
     return out
 
 
-def ring_subrecord(rank, local, world, pg, steps=3, warmup=2):
+def ring_subrecord(rank, local, world, pg, steps=3, warmup=2, clock_path=None):
     """The long-context causal fwd+bwd as a ring over the same ranks (one global problem).
 
     q, k, v, dO (1, 32, 131072, 128) fp16, N(0, 1) like the long-context
@@ -937,12 +937,18 @@ def ring_subrecord(rank, local, world, pg, steps=3, warmup=2):
         comm.wait(stream, timeout_ms=300000)
         ev = [Event() for _ in range(steps + 1)]
         mids = [Event() for _ in range(steps)]
+        clocks = ClockSampler(local, clock_path).start() if clock_path is not None else None
         barrier(pg)
+        if clocks:
+            clocks.mark(0)
         ev[0].record(stream)
         for i in range(steps):
             step(mids[i])
             ev[i + 1].record(stream)
         comm.wait(stream, timeout_ms=300000)
+        if clocks:
+            clocks.mark(1)
+            clocks.stop()
         ms = max_over_ranks(pg, ev[0].elapsed_ms(ev[-1]) / steps, local)
         fwd_ms = max_over_ranks(pg, statistics.mean(ev[i].elapsed_ms(mids[i]) for i in range(steps)), local)
         bwd_ms = max_over_ranks(pg, statistics.mean(mids[i].elapsed_ms(ev[i + 1]) for i in range(steps)), local)
@@ -961,7 +967,8 @@ def ring_subrecord(rank, local, world, pg, steps=3, warmup=2):
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "steps": steps, "warmup": warmup,
             "phase_ms_rank0": phases, "phase_ms_max_over_ranks": phases_max,
             "phase_note": "one extra profiled step; attention + accumulate + repack + wait_nccl "
-                          "is the compute stream's busy time, nccl_transfer overlaps it"}
+                          "is the compute stream's busy time, nccl_transfer overlaps it",
+            "clocks_rank0": clocks.summary() if clocks else None}
 
 
 def run_ring(args, rank, local, world, pg):
