@@ -62,7 +62,9 @@ def _download(st, buf, shape, dtype):
 
 
 @pytest.mark.parametrize("hd,causal,shape", [(128, True, (2, 8, 2, 300, 300)), (64, False, (1, 4, 4, 200, 333)),
-                                             (128, False, (1, 4, 1, 1, 5000))])
+                                             (128, False, (1, 4, 1, 1, 5000)),
+                                             # head dim 40: the exact CUDA-core kernel's bf16 path
+                                             (40, True, (1, 4, 2, 100, 130)), (40, False, (2, 4, 4, 1, 300))])
 def test_bf16_forward_and_decode(hd, causal, shape):
     import pa_b200
     from pa_b200._lib import check, lib
