@@ -199,3 +199,38 @@ def test_gloo_ring(tmp_path, world):
     mp.start_processes(_worker, args=(world, _free_port(), str(result)), nprocs=world, join=True,
                        start_method="spawn")
     assert result.read_text() == "ok"
+
+
+def test_ring_profile_phases_map_to_names(monkeypatch):
+    """RingComm.profile_read returns the five phase times in include/pa_b200.h's
+    PA_RING_PHASE_* order (checked against a fake native library)."""
+    import ctypes
+
+    import pa_b200.ring as ring_mod
+
+    calls = []
+
+    class Fake:
+        def pa_comm_init(self, handle_ref, uid, nranks, rank):
+            return 0
+
+        def pa_comm_profile_start(self, handle):
+            calls.append("start")
+            return 0
+
+        def pa_comm_profile_read(self, handle, ms):
+            arr = ctypes.cast(ms, ctypes.POINTER(ctypes.c_float * 5)).contents
+            for i, v in enumerate((1.5, 100.0, 2.0, 3.0, 40.0)):
+                arr[i] = v
+            calls.append("read")
+            return 0
+
+    monkeypatch.setattr(ring_mod, "lib", lambda: Fake())
+    comm = ring_mod.RingComm(bytes(128), 2, 0)
+    comm.handle = 1
+    comm.profile_start()
+    got = comm.profile_read()
+    assert calls == ["start", "read"]
+    assert got == {"repack": 1.5, "attention": 100.0, "accumulate": 2.0, "wait_nccl": 3.0,
+                   "nccl_transfer": 40.0}
+    comm.handle = None
