@@ -34,6 +34,10 @@ struct pa_comm {
   int nranks, rank, device;
   cudaStream_t side;
   cudaEvent_t ev[4];
+  // Second compute stream of the forward (query chunk 1's pairs) and its
+  // fork / join events.
+  cudaStream_t side2;
+  cudaEvent_t fj[2];
   // Phase timing (pa_comm_profile_start / _read): events recorded at phase
   // boundaries on the compute stream (marks[0]) and the side stream (marks[1]);
   // the time from one mark to the next on a stream belongs to the first mark's
@@ -264,12 +268,14 @@ pa_status pa_comm_init(pa_comm** out, const uint8_t id[128], int32_t nranks, int
     delete c;
     return fail_nccl(r, "ncclCommInitRank");
   }
-  if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess) {
+  if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&c->side2, cudaStreamNonBlocking) != cudaSuccess) {
     g_nccl.CommDestroy(c->nccl);
     delete c;
-    return fail(PA_ERR_CUDA, "pa_comm_init: side stream");
+    return fail(PA_ERR_CUDA, "pa_comm_init: side streams");
   }
   for (auto& e : c->ev) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+  for (auto& e : c->fj) cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
   *out = c;
   return PA_OK;
 }
@@ -277,7 +283,10 @@ pa_status pa_comm_init(pa_comm** out, const uint8_t id[128], int32_t nranks, int
 pa_status pa_comm_destroy(pa_comm* c) {
   if (!c) return PA_OK;
   cudaStreamSynchronize(c->side);
+  cudaStreamSynchronize(c->side2);
   for (auto& e : c->ev) cudaEventDestroy(e);
+  for (auto& e : c->fj) cudaEventDestroy(e);
+  cudaStreamDestroy(c->side2);
   for (auto& e : c->event_pool) cudaEventDestroy(e);
   cudaStreamDestroy(c->side);
   // An aborted communicator (pa_comm_wait) is already freed.
@@ -361,8 +370,9 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
   const int64_t C = sh.C, D = sh.D;
   const size_t qb = sh.q_chunk * es, kvb = sh.kv_chunk * es;
   const int64_t rows = sh.planes_q * C;
-  // scratch: q chunks [2], kv ring buffers [2] x (K0,K1,V0,V1), part out, part lse, acc o [2], acc lse [2]
-  const size_t bytes = 2 * qb + 2 * 4 * kvb + qb + rows * 4 + 2 * rows * D * 4 + 2 * rows * 4 + 4096;
+  // scratch: q chunks [2], kv ring buffers [2] x (K0,K1,V0,V1), part out [2], part lse [2],
+  // acc o [2], acc lse [2] (one part buffer per compute stream)
+  const size_t bytes = 2 * qb + 2 * 4 * kvb + 2 * qb + 2 * rows * 4 + 2 * rows * D * 4 + 2 * rows * 4 + 4096;
   uint8_t* ws = nullptr;
   PA_TRY(scratch_alloc(reinterpret_cast<void**>(&ws), bytes, st));
   auto align = [](size_t x) { return (x + 255) & ~size_t(255); };
@@ -370,8 +380,8 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
   auto take = [&](size_t b) { uint8_t* p = ws + off; off += align(b); return p; };
   uint8_t* qc[2] = {take(qb), take(qb)};
   uint8_t* kvbuf[2] = {take(4 * kvb), take(4 * kvb)};
-  uint8_t* part_o = take(qb);
-  float* part_lse = reinterpret_cast<float*>(take(rows * 4));
+  uint8_t* part_o[2] = {take(qb), take(qb)};
+  float* part_lse[2] = {reinterpret_cast<float*>(take(rows * 4)), reinterpret_cast<float*>(take(rows * 4))};
   float* acc_o[2] = {reinterpret_cast<float*>(take(rows * D * 4)), reinterpret_cast<float*>(take(rows * D * 4))};
   float* acc_l[2] = {reinterpret_cast<float*>(take(rows * 4)), reinterpret_cast<float*>(take(rows * 4))};
   pa_status rc = PA_OK;
@@ -405,25 +415,35 @@ pa_status pa_ring_fwd(pa_comm* comm, const pa_sdpa_desc* desc, const void* q, co
         mark(comm, 1, kPhEnd, comm->side);
         cudaEventRecord(comm->ev[1], comm->side);
       }
+      // The two query chunks' pairs touch disjoint accumulators: chunk 1's run on
+      // a second compute stream beside chunk 0's, so one persistent launch's
+      // tail overlaps the other's work.
+      cudaEventRecord(comm->fj[0], st);
+      cudaStreamWaitEvent(comm->side2, comm->fj[0], 0);
       for (int qw = 0; qw < 2 && rc == PA_OK; ++qw) {
         const int qid = chunk_id(n, r, qw);
+        cudaStream_t sq = qw == 0 ? st : comm->side2;
         for (int kw = 0; kw < 2 && rc == PA_OK; ++kw) {
           const int kid = chunk_id(n, src, kw);
           if (kid > qid) continue;
           pa_sdpa_desc cd = chunk_desc(d, C, kid == qid);
-          mark(comm, 0, kPhAttn, st);
+          if (qw == 0) mark(comm, 0, kPhAttn, st);
           rc = launch_fwd_tc(cd, qc[qw], kvbuf[cur] + kw * kvb, kvbuf[cur] + (2 + kw) * kvb, nullptr,
-                             part_o, part_lse, st);
+                             part_o[qw], part_lse[qw], sq);
           if (rc != PA_OK) break;
-          mark(comm, 0, kPhAccum, st);
+          if (qw == 0) mark(comm, 0, kPhAccum, st);
           if (bf16)
-            ring_merge_kernel<true><<<blocks_for(rows * 32, 256), 256, 0, st>>>(part_o, part_lse, acc_o[qw],
+            ring_merge_kernel<true><<<blocks_for(rows * 32, 256), 256, 0, sq>>>(part_o[qw], part_lse[qw], acc_o[qw],
                                                                                 acc_l[qw], rows, static_cast<int>(D));
           else
-            ring_merge_kernel<false><<<blocks_for(rows * 32, 256), 256, 0, st>>>(part_o, part_lse, acc_o[qw],
+            ring_merge_kernel<false><<<blocks_for(rows * 32, 256), 256, 0, sq>>>(part_o[qw], part_lse[qw], acc_o[qw],
                                                                                  acc_l[qw], rows, static_cast<int>(D));
         }
       }
+      cudaEventRecord(comm->fj[1], comm->side2);
+      mark(comm, 0, kPhAttn, st);  // waiting for chunk 1's pairs
+      cudaStreamWaitEvent(st, comm->fj[1], 0);
+      if (rc != PA_OK) break;
       if (t + 1 < n) {
         mark(comm, 0, kPhWait, st);
         cudaStreamWaitEvent(st, comm->ev[1], 0);
