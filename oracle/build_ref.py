@@ -107,8 +107,9 @@ def import_reference():
     blob = marshal.loads(BUNDLE.read_bytes())
     if tuple(blob.get("python", ())) != sys.version_info[:2]:
         return None
-    if not any(isinstance(f, _BundleFinder) for f in sys.meta_path):
-        sys.meta_path.insert(0, _BundleFinder(blob["modules"]))
+    # One finder, for this bundle (a finder left by an earlier bundle is replaced).
+    sys.meta_path[:] = [f for f in sys.meta_path if not isinstance(f, _BundleFinder)]
+    sys.meta_path.insert(0, _BundleFinder(blob["modules"]))
     return importlib.import_module(PACKAGE)
 
 

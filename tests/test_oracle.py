@@ -206,3 +206,42 @@ def test_acceptance_rule_flags_raising_backend():
 
     ok, detail = oc.check(boom, case)
     assert not ok and "backend raised RuntimeError: boom" in detail
+
+
+def test_reference_bundle_builds_and_imports(tmp_path, monkeypatch):
+    """oracle/build_ref.py byte-compiles a package tree into one code bundle and imports it
+    through its own finder; a bundle for another Python version is ignored."""
+    import marshal
+    import sys
+
+    from oracle import build_ref
+
+    src = tmp_path / "ref" / "src" / build_ref.PACKAGE
+    src.mkdir(parents=True)
+    (src / "__init__.py").write_text("from .mod import answer\n__all__ = ['answer']\n")
+    (src / "mod.py").write_text("def answer():\n    return 42\n")
+    out = tmp_path / "_ref"
+    monkeypatch.setattr(build_ref, "OUT", out)
+    monkeypatch.setattr(build_ref, "BUNDLE", out / (build_ref.PACKAGE + ".codebundle"))
+    monkeypatch.delenv("PA_REFERENCE_SRC", raising=False)
+    saved = {k: sys.modules.pop(k) for k in list(sys.modules) if k.split(".")[0] == build_ref.PACKAGE}
+    saved_path = list(sys.meta_path)
+    try:
+        assert build_ref.build(tmp_path / "ref") == build_ref.BUNDLE
+        assert not list(out.rglob("*.py"))            # code objects only, no sources
+        pkg = build_ref.import_reference()
+        assert pkg.answer() == 42
+        # A bundle written by another Python version is not loaded.
+        for k in [k for k in sys.modules if k.split(".")[0] == build_ref.PACKAGE]:
+            del sys.modules[k]
+        sys.meta_path[:] = saved_path
+        blob = marshal.loads(build_ref.BUNDLE.read_bytes())
+        blob["python"] = (2, 7)
+        build_ref.BUNDLE.write_bytes(marshal.dumps(blob))
+        assert build_ref.import_reference() is None
+        assert build_ref.build(tmp_path / "missing") is None
+    finally:
+        for k in [k for k in sys.modules if k.split(".")[0] == build_ref.PACKAGE]:
+            del sys.modules[k]
+        sys.modules.update(saved)
+        sys.meta_path[:] = saved_path
